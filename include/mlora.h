@@ -1,0 +1,182 @@
+/*
+ * mlora.h - C ABI of the B200-native heterogeneous multi-LoRA linear.
+ *
+ * One frozen backbone W [d_out, d_in] (+ bias [d_out]) is shared by many LoRA
+ * adapters.  Rows of X [rows, d_in] are grouped into contiguous segments; each
+ * segment belongs to one adapter a with rank r_a and scaling s_a = alpha/r_a:
+ *
+ *     Y = X W^T + bias + sum_seg s_a (X_seg A_a^T) B_a^T
+ *
+ * Backward (W frozen, no dW):
+ *     dX = dY W + sum_seg (s_a dY_seg B_a) A_a
+ *     dA_a = sum_seg (s_a dY_seg B_a)^T X_seg,   dB_a = s_a sum_seg dY_seg^T (X_seg A_a^T)
+ *
+ * Adapter weights live in two packed, zero-padded matrices shared by all
+ * adapters: A_pack [r_pack, d_in] holds A_a in rows [pack_off[a], +rank[a]) and
+ * B_pack [d_out, r_pack] holds B_a in columns [pack_off[a], +rank[a]).  Every
+ * pack_off is a multiple of MLORA_RANK_CHUNK, and the rows/columns between
+ * rank[a] and the next chunk boundary must be zero.
+ *
+ * All tensors are dense row-major device memory owned by the caller; every
+ * entry point takes an explicit stream and allocates nothing on the hot path.
+ * Routing arrays (mlora_routing) are HOST arrays.
+ *
+ * Reference interfaces replaced (GOPIKA-SUSHAMA/mini-tlora-reproduction):
+ *   mlora_forward   MultiLoRALinear.forward          tlora/multi_lora_linear.py:92-118
+ *                   fused_full_forward (cuBLAS base + fused_lora_residual_kernel,
+ *                   ADD_BASE=True)                     phase5c_fused_triton.py:545-577,201-300
+ *   mlora_backward  FusedTritonLoRAFunction.backward   phase5d_triton_training.py:248-325
+ *                   plus the autograd of model.base    tlora/multi_lora_linear.py:106
+ *   mlora_sgd       per-adapter isolated SGD step      phase5d_triton_training.py:554-559,
+ *                                                       phase3_nano_batch.py:90-107
+ *   mlora_route_*   boolean-mask routing of ids        tlora/multi_lora_linear.py:111-116
+ *                   and contiguous packing              phase3_nano_batch.py:43-71
+ *   mlora_gather_rows / mlora_scatter_rows  (row permutation for any-order ids)
+ */
+#ifndef MLORA_H
+#define MLORA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MLORA_OK 0
+#define MLORA_ERR_INVALID_ARG 1  /* bad shape, null pointer, inconsistent routing */
+#define MLORA_ERR_UNSUPPORTED 2  /* dtype or alignment this build does not handle */
+#define MLORA_ERR_WORKSPACE 3    /* workspace or save buffer too small */
+#define MLORA_ERR_CUDA 4         /* a CUDA runtime call failed */
+#define MLORA_ERR_DEVICE_FLAG 5  /* a kernel's own bounds check fired */
+#define MLORA_ERR_TIMEOUT 6      /* a bounded device-side wait gave up */
+
+/* element types */
+#define MLORA_F32 0
+#define MLORA_BF16 1
+
+/* adapter ranks are packed in chunks of this many rows/columns */
+#define MLORA_RANK_CHUNK 64
+/* rows per tile of the routing plan */
+#define MLORA_TILE_ROWS 128
+
+/* kernel family selection for mlora_forward / mlora_backward */
+#define MLORA_IMPL_AUTO 0   /* tcgen05 tensor-core kernels when the shape allows, else SIMT */
+#define MLORA_IMPL_SIMT 1   /* CUDA-core kernels, fp32 accumulate (exact fp32 mode) */
+#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only) */
+
+typedef struct mlora_problem {
+  int64_t rows;   /* M: rows of X in this call */
+  int32_t d_in;   /* in_features  (K of the backbone GEMM) */
+  int32_t d_out;  /* out_features (N of the backbone GEMM) */
+  int32_t dtype;  /* MLORA_F32 or MLORA_BF16, for every tensor argument */
+  int32_t impl;   /* MLORA_IMPL_* */
+} mlora_problem;
+
+typedef struct mlora_routing {
+  int32_t n_seg;              /* number of contiguous row segments */
+  const int32_t* seg_start;   /* [n_seg + 1]; seg_start[0] = 0, seg_start[n_seg] = rows, non-decreasing */
+  const int32_t* seg_adapter; /* [n_seg]; adapter slot of each segment, -1 = backbone only */
+  int32_t n_adapters;
+  const int32_t* rank;        /* [n_adapters] true rank r_a >= 1 */
+  const int32_t* pack_off;    /* [n_adapters] first packed row/column, multiple of MLORA_RANK_CHUNK */
+  const float* scaling;       /* [n_adapters] s_a = alpha_a / r_a */
+  int32_t r_pack;             /* packed rank extent, multiple of MLORA_RANK_CHUNK */
+} mlora_routing;
+
+/* Bytes of the forward->backward save buffer (the scaled, per-tile masked
+ * low-rank intermediate s_a * X_seg A_a^T). */
+int mlora_zsave_bytes(const mlora_problem* prob, const mlora_routing* route, size_t* bytes);
+
+/* Bytes of scratch workspace needed by mlora_forward / mlora_backward. */
+int mlora_workspace_bytes(const mlora_problem* prob, const mlora_routing* route, size_t* bytes);
+
+/* Fused forward: Y = X W^T + bias + per-segment LoRA.  bias may be NULL.
+ * W may be NULL: then only the LoRA delta (+ bias) is computed, the
+ * reference kernel's ADD_BASE=False mode (phase5c_fused_triton.py:201-300).
+ * zsave (mlora_zsave_bytes) receives the intermediate the backward needs. */
+int mlora_forward(const mlora_problem* prob, const mlora_routing* route,
+                  const void* X, const void* W, const void* bias,
+                  const void* A_pack, const void* B_pack,
+                  void* Y, void* zsave, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* Analytic backward.  Any of dX, dA_pack, dB_pack may be NULL to skip it.
+ * W may be NULL: then dX holds only the LoRA term (delta-only forward).
+ * dA_pack/dB_pack are written (not accumulated) for every adapter that owns at
+ * least one row; entries of adapters with no rows are left untouched. */
+int mlora_backward(const mlora_problem* prob, const mlora_routing* route,
+                   const void* dY, const void* X, const void* W,
+                   const void* A_pack, const void* B_pack, const void* zsave,
+                   void* dX, void* dA_pack, void* dB_pack,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* One parameter tensor of one adapter for mlora_sgd: a 2-D strided view
+ * P[i * ld_param + j] (i < rows, j < cols) with gradient G[i * ld_grad + j]. */
+typedef struct mlora_sgd_item {
+  void* param;
+  const void* grad;
+  int64_t rows, cols;
+  int64_t ld_param, ld_grad;
+} mlora_sgd_item;
+
+/* Isolated SGD step, P <- P - lr * G, over exactly the listed tensors (one
+ * launch for all of them).  Tensors of adapters that are not listed are
+ * neither read nor written, which is the optimizer isolation of the reference
+ * (one torch.optim.SGD per adapter).  items is a HOST array. */
+int mlora_sgd(const mlora_sgd_item* items, int32_t n_items, float lr, int32_t dtype, void* stream);
+
+/* Routing of per-row adapter ids (int64, device).  adapter_ids_sorted is a
+ * device array of the module's adapter ids in ascending order and
+ * slot_of_sorted the slot of each; a row whose id is not listed maps to -1.
+ * out (device, int32, 2 + 2*max_runs entries) receives
+ *   out[0] = number of maximal runs of equal slot,
+ *   out[1] = rows whose id names no adapter,
+ *   then for r < min(runs, max_runs): out[2+2r] = run start, out[3+2r] = slot,
+ *   in no particular order. */
+int mlora_route_runs(const int64_t* ids, int64_t rows,
+                     const int64_t* adapter_ids_sorted, const int32_t* slot_of_sorted,
+                     int32_t n_adapters, int32_t max_runs, int32_t* out, void* stream);
+
+/* Stable counting sort of rows by slot (slots -1 last).  perm (device, int32
+ * [rows]) receives the source row of each sorted position; counts (device,
+ * int32 [n_adapters + 1]) the rows per slot, slot -1 last.  workspace must
+ * hold mlora_route_sort_workspace_bytes bytes. */
+size_t mlora_route_sort_workspace_bytes(int64_t rows, int32_t n_adapters);
+int mlora_route_sort(const int64_t* ids, int64_t rows,
+                     const int64_t* adapter_ids_sorted, const int32_t* slot_of_sorted,
+                     int32_t n_adapters, int32_t* perm, int32_t* counts,
+                     void* workspace, void* stream);
+
+/* dst[i, :] = src[perm[i], :]  and  dst[perm[i], :] = src[i, :]. */
+int mlora_gather_rows(const void* src, const int32_t* perm, int64_t rows, int32_t cols,
+                      int32_t dtype, void* dst, void* stream);
+int mlora_scatter_rows(const void* src, const int32_t* perm, int64_t rows, int32_t cols,
+                       int32_t dtype, void* dst, void* stream);
+
+/* Device error word of this library on the current device: bit 0 = a bounds
+ * check fired, bit 1 = a bounded wait timed out.  mlora_clear_error resets it. */
+int mlora_get_error(int32_t* flags);
+int mlora_clear_error(void);
+
+/* Number of kernels this library has launched in this process. */
+int64_t mlora_launch_count(void);
+
+/* Per-kernel device timing.  While enabled, every tensor-core kernel launch
+ * is bracketed by CUDA events on its own stream; mlora_timing_read waits for
+ * the recorded events and returns, for kernel role `kind` (0 forward main,
+ * 1 dX main, 2 forward shrink, 3 backward shrink, 4 dA/dB reduction), the
+ * summed device milliseconds and the launch count since the last reset. */
+int mlora_timing_enable(int32_t on);
+int mlora_timing_read(int32_t kind, double* total_ms, int64_t* launches);
+int mlora_timing_reset(void);
+
+/* Human-readable text of a status code. */
+const char* mlora_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLORA_H */

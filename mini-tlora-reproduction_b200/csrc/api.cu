@@ -1,0 +1,201 @@
+// C-ABI entry points (include/mlora.h): argument checks, plan upload and
+// dispatch between the tcgen05 tensor-core family and the SIMT family.
+#include <cstring>
+
+#include "common.cuh"
+#include "simt.cuh"
+#include "tc.cuh"
+
+namespace mlora {
+
+namespace {
+
+size_t zt_bytes(const Plan& p, int dtype) {
+  return size_t(p.chunks.size()) * kTileRows * kChunk * elem_bytes(dtype);
+}
+
+// layout of the caller's workspace: [plan tables | dZt scratch]
+size_t ws_bytes(const Plan& p, int dtype) { return align_up(p.bytes, 1024) + zt_bytes(p, dtype); }
+
+// Copy the plan tables into the workspace (one async H2D from pageable memory,
+// staged before return) and return the device view.
+int upload_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
+  thread_local std::vector<uint8_t> host;
+  host.assign(p.bytes, 0);
+  auto put = [&](size_t off, const void* src, size_t n) {
+    if (n) std::memcpy(host.data() + off, src, n);
+  };
+  put(p.off_tcb, p.tile_chunk_begin.data(), sizeof(int32_t) * p.tile_chunk_begin.size());
+  put(p.off_chunks, p.chunks.data(), sizeof(Chunk) * p.chunks.size());
+  put(p.off_shrink, p.shrink.data(), sizeof(ShrinkItem) * p.shrink.size());
+  put(p.off_reduce, p.reduce.data(), sizeof(ReduceItem) * p.reduce.size());
+  put(p.off_list, p.list.data(), sizeof(int32_t) * p.list.size());
+  MLORA_CUDA_TRY(cudaMemcpyAsync(ws, host.data(), p.bytes, cudaMemcpyHostToDevice, st));
+  uint8_t* b = (uint8_t*)ws;
+  std::memset(dev, 0, sizeof(*dev));
+  dev->n_tiles = p.n_tiles;
+  dev->n_chunks = int32_t(p.chunks.size());
+  dev->n_shrink = int32_t(p.shrink.size());
+  dev->n_reduce = int32_t(p.reduce.size());
+  dev->n_list = int32_t(p.list.size());
+  dev->tile_chunk_begin = (const int32_t*)(b + p.off_tcb);
+  dev->chunks = (const Chunk*)(b + p.off_chunks);
+  dev->shrink = (const ShrinkItem*)(b + p.off_shrink);
+  dev->reduce = (const ReduceItem*)(b + p.off_reduce);
+  dev->list = (const int32_t*)(b + p.off_list);
+  dev->counters = (int32_t*)(b + p.off_counters);
+  return MLORA_OK;
+}
+
+bool tc_shape_ok(const mlora_problem* prob) {
+  // TMA: global strides must be multiples of 16 bytes (bf16: 8 elements)
+  return prob->dtype == MLORA_BF16 && prob->d_in % 8 == 0 && prob->d_out % 8 == 0;
+}
+
+int choose_impl(const mlora_problem* prob) {
+  if (prob->impl == MLORA_IMPL_SIMT) return MLORA_IMPL_SIMT;
+  if (prob->impl == MLORA_IMPL_TC) return tc_shape_ok(prob) ? MLORA_IMPL_TC : -1;
+  if (prob->impl != MLORA_IMPL_AUTO) return -1;
+  return (tc_shape_ok(prob) && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
+}
+
+}  // namespace
+}  // namespace mlora
+
+using namespace mlora;
+
+extern "C" int mlora_zsave_bytes(const mlora_problem* prob, const mlora_routing* route, size_t* bytes) {
+  if (!bytes) return MLORA_ERR_INVALID_ARG;
+  Plan p;
+  int st = build_plan(prob, route, &p);
+  if (st != MLORA_OK) return st;
+  *bytes = zt_bytes(p, prob->dtype);
+  return MLORA_OK;
+}
+
+extern "C" int mlora_workspace_bytes(const mlora_problem* prob, const mlora_routing* route, size_t* bytes) {
+  if (!bytes) return MLORA_ERR_INVALID_ARG;
+  Plan p;
+  int st = build_plan(prob, route, &p);
+  if (st != MLORA_OK) return st;
+  *bytes = ws_bytes(p, prob->dtype);
+  return MLORA_OK;
+}
+
+extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* route, const void* X,
+                             const void* W, const void* bias, const void* A_pack,
+                             const void* B_pack, void* Y, void* zsave, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  thread_local Plan p;
+  int st = build_plan(prob, route, &p);
+  if (st != MLORA_OK) return st;
+  if (prob->rows == 0) return MLORA_OK;
+  if (!X || !Y || !workspace) return MLORA_ERR_INVALID_ARG;
+  if (!p.chunks.empty() && (!A_pack || !B_pack || !zsave)) return MLORA_ERR_INVALID_ARG;
+  if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
+  const int impl = choose_impl(prob);
+  if (impl < 0) return MLORA_ERR_UNSUPPORTED;
+  cudaStream_t s = (cudaStream_t)stream;
+  PlanDev dev;
+  st = upload_plan(p, workspace, s, &dev);
+  if (st != MLORA_OK) return st;
+  if (impl == MLORA_IMPL_TC) {
+    TcCall a;
+    a.plan = dev;
+    a.host = &p;
+    a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+    a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
+    a.Y = Y; a.zsave = zsave;
+    return tc_forward(a, s);
+  }
+  SimtCall a;
+  a.plan = dev;
+  a.n_chunks = dev.n_chunks;
+  a.n_reduce = dev.n_reduce;
+  a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+  a.dtype = prob->dtype;
+  a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
+  a.Y = Y; a.zsave = zsave;
+  return simt_forward(a, s);
+}
+
+extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* route, const void* dY,
+                              const void* X, const void* W, const void* A_pack, const void* B_pack,
+                              const void* zsave, void* dX, void* dA_pack, void* dB_pack,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  thread_local Plan p;
+  int st = build_plan(prob, route, &p);
+  if (st != MLORA_OK) return st;
+  if (prob->rows == 0) return MLORA_OK;
+  if (!dY || !workspace) return MLORA_ERR_INVALID_ARG;
+  if (!p.chunks.empty() && (!A_pack || !B_pack || !zsave)) return MLORA_ERR_INVALID_ARG;
+  if ((dA_pack || dB_pack) && !X) return MLORA_ERR_INVALID_ARG;
+  if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
+  const int impl = choose_impl(prob);
+  if (impl < 0) return MLORA_ERR_UNSUPPORTED;
+  cudaStream_t s = (cudaStream_t)stream;
+  PlanDev dev;
+  st = upload_plan(p, workspace, s, &dev);
+  if (st != MLORA_OK) return st;
+  void* dzt = (uint8_t*)workspace + align_up(p.bytes, 1024);
+  if (impl == MLORA_IMPL_TC) {
+    TcCall a;
+    a.plan = dev;
+    a.host = &p;
+    a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+    a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
+    a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+    return tc_backward(a, s);
+  }
+  SimtCall a;
+  a.plan = dev;
+  a.n_chunks = dev.n_chunks;
+  a.n_reduce = dev.n_reduce;
+  a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+  a.dtype = prob->dtype;
+  a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
+  a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+  return simt_backward(a, s);
+}
+
+extern "C" int mlora_sgd(const mlora_sgd_item* items, int32_t n_items, float lr, int32_t dtype,
+                         void* stream) {
+  if (n_items < 0 || (n_items > 0 && !items)) return MLORA_ERR_INVALID_ARG;
+  if (dtype != MLORA_F32 && dtype != MLORA_BF16) return MLORA_ERR_UNSUPPORTED;
+  for (int i = 0; i < n_items; ++i) {
+    const mlora_sgd_item& it = items[i];
+    if (it.rows < 0 || it.cols < 0) return MLORA_ERR_INVALID_ARG;
+    if (it.rows * it.cols == 0) continue;
+    if (!it.param || !it.grad || it.ld_param < it.cols || it.ld_grad < it.cols) return MLORA_ERR_INVALID_ARG;
+  }
+  return sgd_items(dtype, items, n_items, lr, (cudaStream_t)stream);
+}
+
+extern "C" int mlora_get_error(int32_t* flags) {
+  if (!flags) return MLORA_ERR_INVALID_ARG;
+  int v = 0;
+  MLORA_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_err_word, sizeof(int)));
+  *flags = v;
+  return MLORA_OK;
+}
+
+extern "C" int mlora_clear_error(void) {
+  int z = 0;
+  MLORA_CUDA_TRY(cudaMemcpyToSymbol(g_err_word, &z, sizeof(int)));
+  return MLORA_OK;
+}
+
+extern "C" int64_t mlora_launch_count(void) { return g_launches.load(); }
+
+extern "C" const char* mlora_status_string(int status) {
+  switch (status) {
+    case MLORA_OK: return "ok";
+    case MLORA_ERR_INVALID_ARG: return "invalid argument (shape, pointer or routing)";
+    case MLORA_ERR_UNSUPPORTED: return "unsupported dtype, shape or kernel family";
+    case MLORA_ERR_WORKSPACE: return "workspace or save buffer too small";
+    case MLORA_ERR_CUDA: return "CUDA runtime error";
+    case MLORA_ERR_DEVICE_FLAG: return "device bounds check fired";
+    case MLORA_ERR_TIMEOUT: return "bounded device wait timed out";
+    default: return "unknown status";
+  }
+}

@@ -1,0 +1,9 @@
+// Single translation unit of the mlora native library (keeps device globals
+// such as the error word visible to every kernel without relocatable device
+// code).
+#include "plan.cu"
+#include "timing.cu"
+#include "simt.cu"
+#include "route.cu"
+#include "tc.cu"
+#include "api.cu"

@@ -1,0 +1,26 @@
+// Launch interface of the CUDA-core kernel family.
+#pragma once
+
+#include "common.cuh"
+
+namespace mlora {
+
+struct SimtCall {
+  PlanDev plan;       // device pointers into the workspace
+  int n_chunks = 0;
+  int n_reduce = 0;
+  int64_t M = 0;
+  int d_in = 0, d_out = 0, R = 0, dtype = MLORA_F32;
+  const void *X = nullptr, *W = nullptr, *bias = nullptr, *A_pack = nullptr, *B_pack = nullptr;
+  const void* dY = nullptr;
+  void* Y = nullptr;
+  void* zsave = nullptr;  // Zt (fwd output, bwd input)
+  void* dzt = nullptr;    // dZt scratch (bwd)
+  void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+};
+
+int simt_forward(const SimtCall& a, cudaStream_t st);
+int simt_backward(const SimtCall& a, cudaStream_t st);
+int sgd_items(int dtype, const mlora_sgd_item* items, int n, float lr, cudaStream_t st);
+
+}  // namespace mlora

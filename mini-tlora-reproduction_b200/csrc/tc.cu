@@ -1,0 +1,609 @@
+// tcgen05 / TMEM kernel family of the multi-LoRA linear (sm_100a).
+//
+// One persistent, warp-specialised kernel template serves five roles:
+//
+//   FWD_MAIN    Y  = X W^T + bias + sum_c Zt[c] Bpack[:, chunk c]^T
+//   DX_MAIN     dX = dY W       + sum_c dZt[c] Apack[chunk c, :]
+//   SHRINK_FWD  Zt[c]  = rowmask_c(s_a X_tile Apack[chunk c, :]^T)
+//   SHRINK_BWD  dZt[c] = rowmask_c(s_a dY_tile Bpack[:, chunk c])
+//   REDUCE      dA chunk = sum_tiles dZt[c]^T X_tile,  dB chunk = sum_tiles dY_tile^T Zt[c]
+//
+// The LoRA expand is not a separate pass: each 128-row tile's low-rank
+// blocks Zt[c] (64 rank columns, zero outside the tile rows of the block's
+// segment) are extra K-blocks of the backbone mainloop, accumulated into the
+// same TMEM accumulator, so the full delta-W is never formed and Y is
+// written once.  This replaces the reference's per-row CUDA-core kernel
+// (fused_lora_residual_kernel, phase5c_fused_triton.py:201-300) plus the
+// separate cuBLAS backbone (phase5c_fused_triton.py:555) and the per-adapter
+// PyTorch backward (phase5d_triton_training.py:248-325).
+//
+// Warp roles (192 threads): warp 0 lane 0 issues TMA loads into a 4-stage
+// shared-memory ring; warp 1 owns TMEM (512 columns = two 128x256 fp32
+// accumulators) and lane 0 issues tcgen05.mma; warps 2..5 drain the
+// accumulator of the previous work item (tcgen05.ld) while the next one
+// accumulates.  All operand tiles are 64 bf16 (128 B) wide with the 128-byte
+// swizzle; K-major operands are 128/256-row boxes, MN-major operands are
+// stacks of 64x64 boxes.  No TMA load here uses cluster multicast.
+//
+// Every mbarrier wait is bounded: on timeout the kernel sets the device error
+// word, lets in-flight copies and MMAs land, frees TMEM and returns.
+#include <cuda.h>
+
+#include "tc.cuh"
+
+namespace mlora {
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kABytes = 128 * 64 * 2;  // 16 KB
+constexpr int kBBytes = 256 * 64 * 2;  // 32 KB
+constexpr int kBox64 = 64 * 64 * 2;    // 8 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kTmemCols = 512;
+constexpr int kAccCols = 256;
+constexpr int kGroupM = 16;
+constexpr unsigned long long kTimeoutNs = 2000000000ull;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+
+enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
+
+struct TcParams {
+  CUtensorMap mA0, mB0, mA1, mB1;
+  PlanDev plan;
+  int64_t M;
+  int d_in, d_out, R;
+  int n_items;
+  int n_nblk;   // main modes: 256-wide N blocks
+  int nk_main;  // main / shrink: 64-wide K blocks of the dense part
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* out;  // Y, dX, Zt or dZt
+  __nv_bfloat16* dA;
+  __nv_bfloat16* dB;
+};
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count));
+}
+__device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false if the CTA is aborting or the wait timed out
+// (then the CTA is flagged to abort and the device error word is set).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = su32(b);
+  if (mbar_try(a, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(a, parity)) return true;
+    if ((i & 63) == 63) {
+      if (*abort_flag) return false;
+      if (now_ns() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicOr(&g_err_word, kErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          su32(dst)),
+      "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tc_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
+// version bit.  lbo/sbo in bytes.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = n.
+__device__ __forceinline__ uint32_t idesc_bf16(int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ------------------------------------------------------------------ items
+struct Item {
+  int nk, nk1, n;  // k-blocks total / of the dense part; MMA N
+  int t, nb;       // tile, 256-wide N block
+  int c0, nc;      // chunk range (main: tile's chunks; shrink: item's chunks; reduce: nc)
+  ReduceItem ri;
+  bool skip;
+};
+
+template <int MODE>
+__device__ __forceinline__ Item decode(const TcParams& p, int item) {
+  Item it;
+  it.skip = false;
+  it.nb = 0;
+  if (MODE == FWD_MAIN || MODE == DX_MAIN) {
+    const int per_group = kGroupM * p.n_nblk;
+    const int g = item / per_group, r = item % per_group;
+    const int t0 = g * kGroupM;
+    const int gs = min(kGroupM, p.plan.n_tiles - t0);
+    it.nb = r / gs;
+    it.t = t0 + r % gs;
+    it.c0 = p.plan.tile_chunk_begin[it.t];
+    it.nc = p.plan.tile_chunk_begin[it.t + 1] - it.c0;
+    it.nk1 = p.nk_main;
+    it.nk = it.nk1 + it.nc;
+    it.n = kAccCols;
+  } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
+    const ShrinkItem s = p.plan.shrink[item];
+    it.t = s.tile;
+    it.c0 = s.c0;
+    it.nc = s.nc;
+    it.nk1 = it.nk = p.nk_main;
+    it.n = 64 * s.nc;
+  } else {
+    it.ri = p.plan.reduce[item];
+    it.nc = it.ri.nc;
+    it.nk1 = it.nk = 2 * (it.ri.le - it.ri.lb);
+    it.n = 64 * it.nc;
+    it.t = 0;
+    it.c0 = 0;
+    it.skip = it.ri.kind == 0 ? (p.dA == nullptr) : (p.dB == nullptr);
+  }
+  return it;
+}
+
+// ------------------------------------------------------------------ kernel
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;   // [2]
+  uint64_t* tempty = tfull + 2;        // [2]
+  uint64_t* drain = tempty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr bool A_MN = MODE == REDUCE;
+  constexpr bool B_MN = MODE == DX_MAIN || MODE == SHRINK_BWD || MODE == REDUCE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued_parity[kStages];
+    for (int s = 0; s < kStages; ++s) issued_parity[s] = -1;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+      const Item it = decode<MODE>(p, item);
+      if (it.skip) continue;
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+        uint8_t* sA = smem + stage * kStageBytes;
+        uint8_t* sB = sA + kABytes;
+        uint64_t* bar = &full[stage];
+        if (MODE == FWD_MAIN) {
+          mbar_expect_tx(bar, kABytes + kBBytes);
+          if (kb < it.nk1) {
+            tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+            tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256);
+          } else {
+            const int c = it.c0 + kb - it.nk1;
+            tma_load(sA, &p.mA1, bar, 0, c * 128);
+            tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256);
+          }
+        } else if (MODE == DX_MAIN) {
+          mbar_expect_tx(bar, kABytes + kBBytes);
+          if (kb < it.nk1) {
+            tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64);
+          } else {
+            const int c = it.c0 + kb - it.nk1;
+            const int pcol = p.plan.chunks[c].pcol;
+            tma_load(sA, &p.mA1, bar, 0, c * 128);
+            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol);
+          }
+        } else if (MODE == SHRINK_FWD) {
+          mbar_expect_tx(bar, kABytes + it.nc * kBox64);
+          tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+          for (int i = 0; i < it.nc; ++i)
+            tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol);
+        } else if (MODE == SHRINK_BWD) {
+          mbar_expect_tx(bar, kABytes + it.nc * kBox64);
+          tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+          for (int i = 0; i < it.nc; ++i)
+            tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64);
+        } else {  // REDUCE
+          const int cb = p.plan.list[it.ri.lb + kb / 2];
+          const int h = kb % 2;
+          const int t = p.plan.chunks[cb].tile;
+          const CUtensorMap* ma = it.ri.kind == 0 ? &p.mA0 : &p.mA1;
+          const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
+          mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
+          for (int i = 0; i < 2; ++i) tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * 128 + 64 * h);
+          for (int i = 0; i < it.nc; ++i)
+            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * 128 + 64 * h);
+        }
+        issued_parity[stage] = int(phase);
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) {
+      // let copies already in flight land before the CTA exits
+      const unsigned long long t0 = now_ns();
+      for (int s = 0; s < kStages; ++s) {
+        if (issued_parity[s] < 0) continue;
+        while (!mbar_try(su32(&full[s]), uint32_t(issued_parity[s]))) {
+          if (now_ns() - t0 > kTimeoutNs) break;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    const uint32_t a_lbo = A_MN ? uint32_t(kBox64) : 16u, b_lbo = B_MN ? uint32_t(kBox64) : 16u;
+    const uint32_t a_step = A_MN ? (16 * 128) >> 4 : 32 >> 4;  // descriptor units per UMMA_K = 16
+    const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+      const Item it = decode<MODE>(p, item);
+      if (it.skip) continue;
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + uint32_t(acc * kAccCols);
+      const uint32_t idesc = idesc_bf16(it.n, A_MN, B_MN);
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sA = su32(smem + stage * kStageBytes);
+        const uint64_t ad = sdesc(sA, a_lbo, 1024);
+        const uint64_t bd = sdesc(sA + kABytes, b_lbo, 1024);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma(d, ad + uint64_t(k * a_step), bd + uint64_t(k * b_step), idesc, (kb | k) != 0);
+        tc_commit(&empty[stage]);
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    // every issued MMA has completed once this commit lands
+    tc_commit(drain);
+    const unsigned long long t0 = now_ns();
+    while (!mbar_try(su32(drain), 0)) {
+      if (now_ns() - t0 > kTimeoutNs) { atomicOr(&g_err_word, kErrTimeout); break; }
+    }
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp % 4;
+    const int r = quad * 32 + lane;  // accumulator row = TMEM lane
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+      const Item it = decode<MODE>(p, item);
+      if (it.skip) continue;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);
+      uint32_t v[32];
+      if (MODE == FWD_MAIN || MODE == DX_MAIN) {
+        const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
+        const int64_t row = int64_t(it.t) * 128 + r;
+        const int n0 = it.nb * 256;
+        const bool empty_acc = it.nk == 0;  // delta-only call on a tile without LoRA rows
+        for (int col = 0; col < kAccCols; col += 32) {
+          if (n0 + col >= N) break;
+          if (!empty_acc) tc_ld32(tbase + col, v);
+          if (row >= p.M) continue;
+          float f[32];
+#pragma unroll
+          for (int q = 0; q < 32; ++q) f[q] = empty_acc ? 0.f : __uint_as_float(v[q]);
+          if (MODE == FWD_MAIN && p.bias) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
+          }
+          __nv_bfloat16* dst = p.out + row * N + n0 + col;
+          if (n0 + col + 32 <= N) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                                 pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+          } else {
+            for (int q = 0; q < 32 && n0 + col + q < N; ++q) dst[q] = __float2bfloat16_rn(f[q]);
+          }
+        }
+      } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
+        for (int i = 0; i < it.nc; ++i) {
+          const Chunk ch = p.plan.chunks[it.c0 + i];
+          const bool in = r >= ch.lo && r < ch.hi;
+          __nv_bfloat16* dst = p.out + (int64_t(it.c0 + i) * 128 + r) * 64;
+          for (int col = 0; col < 64; col += 32) {
+            tc_ld32(tbase + i * 64 + col, v);
+            float f[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) f[q] = in ? ch.scale * __uint_as_float(v[q]) : 0.f;
+            uint4* d4 = reinterpret_cast<uint4*>(dst + col);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                                 pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+          }
+        }
+      } else {  // REDUCE
+        const ReduceItem ri = it.ri;
+        const int d = ri.block * 128 + r;
+        const int cb = p.plan.list[ri.lb];
+        for (int i = 0; i < it.nc; ++i) {
+          const int j = ri.j0 + i;
+          const int pcol = p.plan.chunks[cb + j].pcol;
+          const int rvalid = ri.rank - j * 64;
+          for (int col = 0; col < 64; col += 32) {
+            tc_ld32(tbase + i * 64 + col, v);
+            if (ri.kind == 1) {
+              if (d >= p.d_out) continue;
+              __nv_bfloat16* dst = p.dB + int64_t(d) * p.R + pcol + col;
+              if (col + 32 <= rvalid) {
+                uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  d4[q] = make_uint4(pack_bf16(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])),
+                                     pack_bf16(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
+                                     pack_bf16(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
+                                     pack_bf16(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+              } else {
+                for (int q = 0; q < 32 && col + q < rvalid; ++q) dst[q] = __float2bfloat16_rn(__uint_as_float(v[q]));
+              }
+            } else {
+              if (d >= p.d_in) continue;
+              for (int q = 0; q < 32 && col + q < rvalid; ++q)
+                p.dA[int64_t(pcol + col + q) * p.d_in + d] = __float2bfloat16_rn(__uint_as_float(v[q]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static EncodeFn fn = []() -> EncodeFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeFn>(f);
+  }();
+  return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix; box = 64 columns x box_rows
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeFn enc = get_encode();
+  if (!enc || rows < 1 || cols < 1) return false;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (cols * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols * 2)};
+  cuuint32_t box[2] = {64u, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+template <int MODE>
+int launch(TcParams& prm, cudaStream_t st) {
+  if (prm.n_items <= 0) return MLORA_OK;
+  const int sms = num_sms();
+  if (sms <= 0) return MLORA_ERR_CUDA;
+  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  const int grid = prm.n_items < sms ? prm.n_items : sms;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  const bool timed = timing_begin(st, ev);
+  k_tc<MODE><<<grid, kThreads, kSmemBytes, st>>>(prm);
+  count_launch();
+  if (timed) timing_end(MODE, st, ev);
+  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+TcParams base_params(const TcCall& a) {
+  TcParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.plan = a.plan;
+  prm.M = a.M;
+  prm.d_in = a.d_in;
+  prm.d_out = a.d_out;
+  prm.R = a.R;
+  return prm;
+}
+
+}  // namespace
+
+bool tc_available() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10 && get_encode() != nullptr;
+}
+
+int tc_forward(const TcCall& a, cudaStream_t st) {
+  const int n_chunks = a.plan.n_chunks;
+  const int64_t zrows = int64_t(n_chunks) * 128;
+  if (n_chunks > 0) {
+    TcParams prm = base_params(a);
+    if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || !make_map(&prm.mB0, a.A_pack, a.R, a.d_in, 64))
+      return MLORA_ERR_UNSUPPORTED;
+    prm.n_items = a.plan.n_shrink;
+    prm.nk_main = (a.d_in + 63) / 64;
+    prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
+    int s = launch<SHRINK_FWD>(prm, st);
+    if (s != MLORA_OK) return s;
+  }
+  TcParams prm = base_params(a);
+  if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, 256)))
+    return MLORA_ERR_UNSUPPORTED;
+  if (n_chunks > 0 &&
+      (!make_map(&prm.mA1, a.zsave, zrows, 64, 128) || !make_map(&prm.mB1, a.B_pack, a.d_out, a.R, 256)))
+    return MLORA_ERR_UNSUPPORTED;
+  prm.n_nblk = (a.d_out + 255) / 256;
+  prm.n_items = a.plan.n_tiles * prm.n_nblk;
+  prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
+  prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
+  return launch<FWD_MAIN>(prm, st);
+}
+
+int tc_backward(const TcCall& a, cudaStream_t st) {
+  const int n_chunks = a.plan.n_chunks;
+  const int64_t zrows = int64_t(n_chunks) * 128;
+  int s;
+  if (n_chunks > 0 && (a.dX || a.dA)) {
+    TcParams prm = base_params(a);
+    if (!make_map(&prm.mA0, a.dY, a.M, a.d_out, 128) || !make_map(&prm.mB0, a.B_pack, a.d_out, a.R, 64))
+      return MLORA_ERR_UNSUPPORTED;
+    prm.n_items = a.plan.n_shrink;
+    prm.nk_main = (a.d_out + 63) / 64;
+    prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
+    if ((s = launch<SHRINK_BWD>(prm, st)) != MLORA_OK) return s;
+  }
+  if (a.dX) {
+    TcParams prm = base_params(a);
+    if (!make_map(&prm.mA0, a.dY, a.M, a.d_out, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, 64)))
+      return MLORA_ERR_UNSUPPORTED;
+    if (n_chunks > 0 &&
+        (!make_map(&prm.mA1, a.dzt, zrows, 64, 128) || !make_map(&prm.mB1, a.A_pack, a.R, a.d_in, 64)))
+      return MLORA_ERR_UNSUPPORTED;
+    prm.n_nblk = (a.d_in + 255) / 256;
+    prm.n_items = a.plan.n_tiles * prm.n_nblk;
+    prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
+    prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
+    if ((s = launch<DX_MAIN>(prm, st)) != MLORA_OK) return s;
+  }
+  if (n_chunks > 0 && (a.dA || a.dB)) {
+    TcParams prm = base_params(a);
+    if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 64) || !make_map(&prm.mB0, a.dzt, zrows, 64, 64) ||
+        !make_map(&prm.mA1, a.dY, a.M, a.d_out, 64) || !make_map(&prm.mB1, a.zsave, zrows, 64, 64))
+      return MLORA_ERR_UNSUPPORTED;
+    prm.n_items = a.plan.n_reduce;
+    prm.dA = reinterpret_cast<__nv_bfloat16*>(a.dA);
+    prm.dB = reinterpret_cast<__nv_bfloat16*>(a.dB);
+    if ((s = launch<REDUCE>(prm, st)) != MLORA_OK) return s;
+  }
+  return MLORA_OK;
+}
+
+}  // namespace mlora

@@ -1,0 +1,28 @@
+// Launch interface of the tcgen05 / TMEM tensor-core kernel family (bf16 in,
+// fp32 accumulate in tensor memory, operands staged by TMA).
+#pragma once
+
+#include "common.cuh"
+
+namespace mlora {
+
+struct TcCall {
+  PlanDev plan;
+  const Plan* host = nullptr;
+  int64_t M = 0;
+  int d_in = 0, d_out = 0, R = 0;
+  const void *X = nullptr, *W = nullptr, *bias = nullptr, *A_pack = nullptr, *B_pack = nullptr;
+  const void* dY = nullptr;
+  void* Y = nullptr;
+  void* zsave = nullptr;
+  void* dzt = nullptr;
+  void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+};
+
+// true when the driver exposes cuTensorMapEncodeTiled and the current device
+// is an sm_100 part
+bool tc_available();
+int tc_forward(const TcCall& a, cudaStream_t st);
+int tc_backward(const TcCall& a, cudaStream_t st);
+
+}  // namespace mlora

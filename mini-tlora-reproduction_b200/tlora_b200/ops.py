@@ -1,0 +1,334 @@
+"""Functional layer over the C ABI: routing, the fused forward/backward
+autograd function and the isolated SGD step.
+
+Reference call sites this mirrors:
+  * boolean-mask routing          tlora/multi_lora_linear.py:111-116
+  * contiguous packing (spans)    phase3_nano_batch.py:43-71, phase5c_fused_triton.py:338-377
+  * fused kernel + autograd       phase5c_fused_triton.py:545-577, phase5d_triton_training.py:196-325
+  * per-adapter SGD               phase5d_triton_training.py:554-559, phase3_nano_batch.py:90-107
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, RANK_CHUNK, TILE_ROWS
+
+_DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
+_IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC}
+
+
+def mlora_dtype(dt: torch.dtype) -> int:
+    if dt not in _DTYPES:
+        raise NotImplementedError(f"dtype {dt} is not supported (float32 or bfloat16)")
+    return _DTYPES[dt]
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+# ---------------------------------------------------------------------------
+# adapter table: ranks, packed offsets, scaling
+# ---------------------------------------------------------------------------
+
+@dataclass
+class AdapterTable:
+    """Packed layout of a set of adapters: adapter ``ids[i]`` (slot i) owns
+    rows [pack_off[i], pack_off[i] + rank[i]) of A_pack and the same columns
+    of B_pack; every offset is a multiple of RANK_CHUNK."""
+
+    ids: List[int]
+    rank: np.ndarray      # int32 [n]
+    pack_off: np.ndarray  # int32 [n]
+    r_pack: int
+    _dev_keys: dict = field(default_factory=dict, repr=False)
+
+    @staticmethod
+    def build(ids: Sequence[int], ranks: Sequence[int]) -> "AdapterTable":
+        rank = np.asarray(list(ranks), dtype=np.int32)
+        pad = (rank + RANK_CHUNK - 1) // RANK_CHUNK * RANK_CHUNK
+        off = np.zeros(len(rank), dtype=np.int32)
+        if len(rank):
+            off[1:] = np.cumsum(pad)[:-1]
+        return AdapterTable(list(int(i) for i in ids), rank, off, int(pad.sum()))
+
+    @property
+    def n(self) -> int:
+        return len(self.ids)
+
+    def slot_of(self) -> dict:
+        return {a: i for i, a in enumerate(self.ids)}
+
+    def device_keys(self, device: torch.device):
+        """(sorted adapter ids int64, slot of each int32) on ``device``."""
+        key = str(device)
+        if key not in self._dev_keys:
+            order = np.argsort(np.asarray(self.ids, dtype=np.int64), kind="stable")
+            keys = torch.tensor(np.asarray(self.ids, dtype=np.int64)[order], device=device)
+            slots = torch.tensor(order.astype(np.int32), device=device)
+            self._dev_keys[key] = (keys, slots)
+        return self._dev_keys[key]
+
+
+# ---------------------------------------------------------------------------
+# routing: per-row ids -> contiguous segments (+ optional permutation)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class RoutePlan:
+    rows: int
+    seg_start: np.ndarray    # int32 [n_seg + 1]
+    seg_adapter: np.ndarray  # int32 [n_seg], slot or -1
+    perm: Optional[torch.Tensor] = None  # int32 [rows] on device: sorted position -> source row
+    active: np.ndarray = None            # bool [n_adapters]: adapter owns >= 1 row
+
+    @property
+    def n_seg(self) -> int:
+        return len(self.seg_adapter)
+
+
+def _segments_from_runs(starts: np.ndarray, slots: np.ndarray, rows: int, n: int) -> RoutePlan:
+    order = np.argsort(starts, kind="stable")
+    starts, slots = starts[order], slots[order]
+    seg_start = np.append(starts, rows).astype(np.int32)
+    seg_adapter = slots.astype(np.int32)
+    active = np.zeros(n, dtype=bool)
+    active[seg_adapter[seg_adapter >= 0]] = True
+    return RoutePlan(rows, seg_start, seg_adapter, None, active)
+
+
+def _segments_from_counts(counts: np.ndarray, n: int, rows: int, perm: torch.Tensor) -> RoutePlan:
+    # sorted order: slot 0..n-1, then rows with unknown ids
+    starts = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    keep = [s for s in range(n + 1) if counts[s] > 0]
+    seg_start = np.array([starts[s] for s in keep] + [rows], dtype=np.int32)
+    seg_adapter = np.array([s if s < n else -1 for s in keep], dtype=np.int32)
+    active = counts[:n] > 0
+    return RoutePlan(rows, seg_start, seg_adapter, perm, active)
+
+
+def _use_runs(n_runs: int, run_slots: np.ndarray, rows: int) -> bool:
+    n_tiles = max(1, (rows + TILE_ROWS - 1) // TILE_ROWS)
+    grouped = n_runs == len(np.unique(run_slots))  # every adapter appears in one run
+    return grouped or n_runs <= n_tiles
+
+
+def route(ids: torch.Tensor, table: AdapterTable, device: torch.device) -> RoutePlan:
+    """Segments for per-row adapter ids.  Ids already grouped (each adapter in
+    one contiguous run, the packed layout of the reference's phase3-6 scripts)
+    are used in place; interleaved ids are stably sorted by adapter, and the
+    plan carries the permutation that gathers X / scatters Y."""
+    rows = int(ids.shape[0])
+    n = table.n
+    if rows == 0:
+        return RoutePlan(0, np.zeros(1, np.int32), np.zeros(0, np.int32), None, np.zeros(n, bool))
+    if ids.device.type != "cuda":
+        # host ids: routing is host logic on an O(rows) integer array
+        slot_of = table.slot_of()
+        v = ids.detach().cpu().numpy().astype(np.int64)
+        uniq, inv = np.unique(v, return_inverse=True)
+        slots = np.array([slot_of.get(int(u), -1) for u in uniq], dtype=np.int32)[inv]
+        head = np.ones(rows, dtype=bool)
+        head[1:] = slots[1:] != slots[:-1]
+        starts = np.nonzero(head)[0]
+        if _use_runs(len(starts), slots[starts], rows):
+            return _segments_from_runs(starts, slots[starts], rows, n)
+        key = np.where(slots < 0, n, slots)
+        order = np.argsort(key, kind="stable").astype(np.int32)
+        counts = np.bincount(key, minlength=n + 1)
+        perm = torch.from_numpy(order).to(device)
+        return _segments_from_counts(counts, n, rows, perm)
+
+    ids64 = ids if ids.dtype == torch.int64 else ids.to(torch.int64)
+    ids64 = ids64.contiguous()
+    keys, slots_d = table.device_keys(ids.device)
+    n_tiles = (rows + TILE_ROWS - 1) // TILE_ROWS
+    max_runs = max(64, 2 * n + 2, n_tiles)
+    out = torch.empty(2 + 2 * max_runs, dtype=torch.int32, device=ids.device)
+    st = _stream(ids.device)
+    _lib.call("mlora_route_runs", _ptr(ids64), rows, _ptr(keys), _ptr(slots_d), n, max_runs, _ptr(out), st)
+    h = out.cpu().numpy()
+    n_runs = int(h[0])
+    if n_runs <= max_runs:
+        starts = h[2:2 + 2 * n_runs:2].astype(np.int64)
+        rs = h[3:3 + 2 * n_runs:2].astype(np.int32)
+        if _use_runs(n_runs, rs, rows):
+            return _segments_from_runs(starts, rs, rows, n)
+    perm = torch.empty(rows, dtype=torch.int32, device=ids.device)
+    counts = torch.empty(n + 1, dtype=torch.int32, device=ids.device)
+    ws = torch.empty(max(1, _lib.lib().mlora_route_sort_workspace_bytes(rows, n)), dtype=torch.uint8,
+                     device=ids.device)
+    _lib.call("mlora_route_sort", _ptr(ids64), rows, _ptr(keys), _ptr(slots_d), n, _ptr(perm), _ptr(counts),
+              _ptr(ws), st)
+    return _segments_from_counts(counts.cpu().numpy().astype(np.int64), n, rows, perm)
+
+
+def gather_rows(src: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    dst = torch.empty_like(src)
+    _lib.call("mlora_gather_rows", _ptr(src), _ptr(perm), src.shape[0], src.shape[1], mlora_dtype(src.dtype),
+              _ptr(dst), _stream(src.device))
+    return dst
+
+
+def scatter_rows(src: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    dst = torch.empty_like(src)
+    _lib.call("mlora_scatter_rows", _ptr(src), _ptr(perm), src.shape[0], src.shape[1], mlora_dtype(src.dtype),
+              _ptr(dst), _stream(src.device))
+    return dst
+
+
+# ---------------------------------------------------------------------------
+# C structs for one call
+# ---------------------------------------------------------------------------
+
+class _CallArgs:
+    """Keeps the numpy arrays behind the ctypes structs alive for one call."""
+
+    def __init__(self, rows, d_in, d_out, dtype, impl, plan: RoutePlan, table: AdapterTable,
+                 scaling: np.ndarray):
+        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl])
+        self.seg_start = np.ascontiguousarray(plan.seg_start, dtype=np.int32)
+        self.seg_adapter = np.ascontiguousarray(plan.seg_adapter, dtype=np.int32)
+        self.rank = np.ascontiguousarray(table.rank, dtype=np.int32)
+        self.pack_off = np.ascontiguousarray(table.pack_off, dtype=np.int32)
+        self.scaling = np.ascontiguousarray(scaling, dtype=np.float32)
+        self.route = _lib.Routing(
+            len(self.seg_adapter), _lib.i32_ptr(self.seg_start), _lib.i32_ptr(self.seg_adapter),
+            table.n, _lib.i32_ptr(self.rank), _lib.i32_ptr(self.pack_off), _lib.f32_ptr(self.scaling),
+            table.r_pack)
+
+    def sizes(self):
+        z = ctypes.c_size_t(0)
+        w = ctypes.c_size_t(0)
+        _lib.call("mlora_zsave_bytes", ctypes.byref(self.prob), ctypes.byref(self.route), ctypes.byref(z))
+        _lib.call("mlora_workspace_bytes", ctypes.byref(self.prob), ctypes.byref(self.route), ctypes.byref(w))
+        return int(z.value), int(w.value)
+
+
+@dataclass
+class LayerState:
+    """Everything the autograd function needs besides the differentiable inputs."""
+
+    table: AdapterTable
+    scaling: np.ndarray
+    plan: RoutePlan
+    A_pack: torch.Tensor
+    B_pack: torch.Tensor
+    impl: str = "auto"
+
+
+def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
+    """Run mlora_forward; returns (Y in the caller's row order, zsave, x in
+    sorted order, call args)."""
+    rows, d_in = x.shape
+    d_out = st.B_pack.shape[0]
+    xs = x_sorted if x_sorted is not None else (gather_rows(x, st.plan.perm) if st.plan.perm is not None else x)
+    args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling)
+    zb, wb = args.sizes()
+    dev = x.device
+    y = torch.empty(rows, d_out, dtype=x.dtype, device=dev)
+    z = torch.empty(max(zb, 1), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+    _lib.call("mlora_forward", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(xs), _ptr(W), _ptr(bias),
+              _ptr(st.A_pack), _ptr(st.B_pack), _ptr(y), _ptr(z), _ptr(ws), wb, _stream(dev))
+    if st.plan.perm is not None:
+        y = scatter_rows(y, st.plan.perm)
+    return y, z, xs, args
+
+
+def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, want_dB: bool):
+    """Run mlora_backward; returns (dX in the caller's row order or None,
+    dA_pack or None, dB_pack or None)."""
+    rows = dy.shape[0]
+    d_in = st.A_pack.shape[1]
+    d_out = st.B_pack.shape[0]
+    dev = dy.device
+    dys = gather_rows(dy, st.plan.perm) if st.plan.perm is not None else dy
+    args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling)
+    _, wb = args.sizes()
+    ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+    dx = torch.empty(rows, d_in, dtype=dy.dtype, device=dev) if want_dx else None
+    # every rank row / column of an adapter that owns rows is written; the
+    # rest is never exposed (inactive adapters get None gradients)
+    dA = torch.empty_like(st.A_pack) if want_dA else None
+    dB = torch.empty_like(st.B_pack) if want_dB else None
+    _lib.call("mlora_backward", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(dys), _ptr(xs), _ptr(W),
+              _ptr(st.A_pack), _ptr(st.B_pack), _ptr(z), _ptr(dx), _ptr(dA), _ptr(dB), _ptr(ws), wb,
+              _stream(dev))
+    if dx is not None and st.plan.perm is not None:
+        dx = scatter_rows(dx, st.plan.perm)
+    return dx, dA, dB
+
+
+class MultiLoRAFunction(torch.autograd.Function):
+    """Y = X W^T + b + per-segment LoRA, with the analytic backward.
+
+    Inputs after ``state``: the per-adapter parameters (A_0, B_0, A_1, ...)
+    as views into the packed buffers; gradients are returned for them, so
+    autograd accumulates into each adapter's ``.grad`` exactly as for the
+    reference module (tlora/multi_lora_linear.py:89-90; grads of adapters
+    that own no rows stay None)."""
+
+    @staticmethod
+    def forward(ctx, x, W, bias, st: LayerState, *adapter_params):
+        y, z, xs, _ = forward_raw(x, W, bias, st)
+        ctx.st = st
+        ctx.save_for_backward(xs, z, W, st.A_pack, st.B_pack)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xs, z, W, _, _ = ctx.saved_tensors
+        st: LayerState = ctx.st
+        n = st.table.n
+        need = ctx.needs_input_grad
+        want_dx = need[0]
+        want_A = any(need[4 + 2 * i] for i in range(n))
+        want_B = any(need[5 + 2 * i] for i in range(n))
+        dx, dA, dB = backward_raw(dy.contiguous(), xs, W, z, st, want_dx, want_A, want_B)
+        grads = []
+        for i in range(n):
+            o, r = int(st.table.pack_off[i]), int(st.table.rank[i])
+            act = bool(st.plan.active[i])
+            grads.append(dA[o:o + r] if (act and dA is not None and need[4 + 2 * i]) else None)
+            grads.append(dB[:, o:o + r] if (act and dB is not None and need[5 + 2 * i]) else None)
+        return (dx, None, None, None, *grads)
+
+
+def sgd_step_(params_and_grads, lr: float) -> int:
+    """P <- P - lr * G for the listed (param, grad) pairs in one launch per 64
+    tensors (mlora_sgd).  Params are 2-D views with unit column stride."""
+    items = []
+    dtype = None
+    device = None
+    keep = []
+    for p, g in params_and_grads:
+        if g is None:
+            continue
+        if p.dim() != 2 or p.stride(1) != 1 or g.stride(1) != 1:
+            raise ValueError("sgd_step_ expects 2-D tensors with unit column stride")
+        if g.dtype != p.dtype or g.shape != p.shape:
+            raise ValueError("gradient must match the parameter's shape and dtype")
+        dt = mlora_dtype(p.dtype)
+        if dtype is None:
+            dtype, device = dt, p.device
+        elif dt != dtype or p.device != device:
+            raise ValueError("all tensors of one sgd_step_ call share a dtype and a device")
+        keep.append(g)
+        items.append(_lib.SgdItem(p.data_ptr(), g.data_ptr(), p.shape[0], p.shape[1], p.stride(0), g.stride(0)))
+    if not items:
+        return 0
+    arr = (_lib.SgdItem * len(items))(*items)
+    _lib.call("mlora_sgd", arr, len(items), float(lr), dtype, _stream(device))
+    return len(items)

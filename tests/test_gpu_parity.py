@@ -1,0 +1,232 @@
+"""GPU parity: the native kernels against the numpy oracle (and, for the
+reference's own test cases, against the reference's golden outputs).
+
+Tolerances (north star): relative L2 <= 1e-5 in fp32 mode, <= 2e-2 in bf16
+mode (fp32 accumulation), for Y, dX, dA, dB and the one-step SGD update.
+"""
+
+import copy
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import mlora_oracle as orc
+from _util import assert_parity, module_step, oracle_step, to_np
+
+from tlora_b200 import MultiLoRALinear, IndependentLoRALinear
+from tlora_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_TOL = 2e-2
+DEV = "cuda"
+
+
+def _golden_module(z):
+    ranks = {int(a): int(z[f"A_{int(a)}"].shape[0]) for a in z["adapter_ids"]}
+    d_out, d_in = z["W"].shape
+    m = MultiLoRALinear(d_in, d_out, ranks, bias="bias" in z)
+    with torch.no_grad():
+        m.base.weight.copy_(torch.from_numpy(z["W"]))
+        if "bias" in z:
+            m.base.bias.copy_(torch.from_numpy(z["bias"]))
+        for a in ranks:
+            ad = m.adapters[str(a)]
+            ad.A.copy_(torch.from_numpy(z[f"A_{a}"]))
+            ad.B.copy_(torch.from_numpy(z[f"B_{a}"]))
+            ad.scaling = float(z[f"scaling_{a}"])
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize("name", ["fwd_equiv", "grad_equiv", "isolation", "cfg0_small", "ragged"])
+@pytest.mark.parametrize("ids_on", ["cpu", "cuda"])
+def test_golden_fp32(golden_dir, name, ids_on):
+    """The reference's own cases (tests/test_equivalence.py shapes and seeds),
+    fp32, against the reference's outputs."""
+    z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    m = _golden_module(z)
+    x = torch.from_numpy(z["x"]).to(DEV).requires_grad_(True)
+    ids = torch.from_numpy(z["ids"]).to(ids_on)
+    y = m(x, ids)
+    loss = torch.nn.functional.mse_loss(y, torch.from_numpy(z["target"]).to(DEV), reduction="sum")
+    loss.backward()
+    assert orc.relative_l2(to_np(y), z["Y"]) <= F32_TOL
+    assert orc.relative_l2(to_np(x.grad), z["dX"]) <= F32_TOL
+    for a in z["adapter_ids"]:
+        a = int(a)
+        ad = m.adapters[str(a)]
+        if f"dA_{a}" in z:
+            assert orc.relative_l2(to_np(ad.A.grad), z[f"dA_{a}"]) <= F32_TOL
+            assert orc.relative_l2(to_np(ad.B.grad), z[f"dB_{a}"]) <= F32_TOL
+        else:
+            assert ad.A.grad is None and ad.B.grad is None
+    # isolated SGD with the reference's optimizer usage and with the fused step
+    lr = float(z["lr"])
+    opt_ids = [int(a) for a in z["opt_ids"]]
+    m2 = copy.deepcopy(m)
+    opts = [torch.optim.SGD(m.adapter_parameters(a), lr=lr) for a in opt_ids]
+    for o in opts:
+        o.step()
+    m2.sgd_step(lr, opt_ids)
+    torch.cuda.synchronize()
+    for a in z["adapter_ids"]:
+        a = int(a)
+        for mm in (m, m2):
+            ad = mm.adapters[str(a)]
+            assert orc.relative_l2(to_np(ad.A), z[f"A_next_{a}"]) <= F32_TOL
+            assert orc.relative_l2(to_np(ad.B), z[f"B_next_{a}"]) <= F32_TOL
+            if a not in opt_ids or f"dA_{a}" not in z:
+                # isolation: bit-identical (tests/test_equivalence.py:137-141)
+                assert np.array_equal(ad.A.detach().cpu().numpy(), z[f"A_{a}"])
+                assert np.array_equal(ad.B.detach().cpu().numpy(), z[f"B_{a}"])
+
+
+def test_reference_equivalence_suite_on_gpu():
+    """tests/test_equivalence.py:17-99 rerun with the new module on the GPU:
+    shared vs independent forward and adapter gradients, 1e-6."""
+    torch.manual_seed(7)
+    ranks = {0: 2, 1: 4, 2: 8}
+    shared = MultiLoRALinear(16, 12, ranks)
+    refs = {aid: IndependentLoRALinear(16, 12, r) for aid, r in ranks.items()}
+    for aid, ref in refs.items():
+        ref.base.weight.data.copy_(shared.base.weight.data)
+        ref.base.bias.data.copy_(shared.base.bias.data)
+        ref.adapter.A.data.copy_(shared.adapters[str(aid)].A.data)
+    for ad in shared.adapters.values():
+        torch.nn.init.normal_(ad.B, mean=0.0, std=0.02)
+    for aid, ref in refs.items():
+        ref.adapter.B.data.copy_(shared.adapters[str(aid)].B.data)
+    shared = shared.to(DEV)
+    refs = {a: r.to(DEV) for a, r in refs.items()}
+    x = torch.randn(12, 16, device=DEV)
+    ids = torch.tensor([0, 0, 1, 2, 1, 0, 2, 2, 1, 0, 1, 2], device=DEV)
+    target = torch.randn(12, 12, device=DEV)
+    y = shared(x, ids)
+    torch.nn.functional.mse_loss(y, target, reduction="sum").backward()
+    y_ref = torch.empty_like(y)
+    for aid, ref in refs.items():
+        mask = ids == aid
+        yr = ref(x[mask])
+        y_ref[mask] = yr.detach()
+        torch.nn.functional.mse_loss(yr, target[mask], reduction="sum").backward()
+        sa = shared.adapters[str(aid)]
+        assert torch.allclose(sa.A.grad, ref.adapter.A.grad, atol=1e-6, rtol=1e-6)
+        assert torch.allclose(sa.B.grad, ref.adapter.B.grad, atol=1e-6, rtol=1e-6)
+    assert torch.allclose(y, y_ref, atol=1e-6, rtol=1e-6)
+
+
+def test_config0_fp32_full_size():
+    """Config 0 at its full size (640 rows, 1024 x 1024) in fp32 mode."""
+    w = workloads.build(workloads.spec("c0"), device=DEV)
+    got = module_step(w.model, w.x, w.ids, w.dy)
+    want = oracle_step(w.model, w.x, w.ids, w.dy)
+    assert_parity(got, want, F32_TOL, "c0 fp32")
+    # one SGD step, lr 1e-3
+    m = w.model
+    before = {k: (to_np(a.A), to_np(a.B)) for k, a in m.adapters.items()}
+    m.sgd_step(w.spec.lr)
+    torch.cuda.synchronize()
+    for k, a in m.adapters.items():
+        A_next = orc.sgd_step(before[k][0], want[2][int(k)], w.spec.lr)
+        B_next = orc.sgd_step(before[k][1], want[3][int(k)], w.spec.lr)
+        assert orc.relative_l2(to_np(a.A), A_next) <= F32_TOL
+        assert orc.relative_l2(to_np(a.B), B_next) <= F32_TOL
+
+
+@pytest.mark.parametrize("cfg,scale", [("c1", 0.125), ("c2", 0.0625), ("c3", 0.0625), ("c4", 0.03125)])
+@pytest.mark.parametrize("impl", ["tc", "simt"])
+def test_bf16_configs_scaled(cfg, scale, impl):
+    """bf16 configurations at reduced size: native kernels vs the fp64 oracle
+    on the same bf16-rounded inputs."""
+    w = workloads.build(workloads.spec(cfg, scale), device=DEV)
+    w.model.impl = impl
+    got = module_step(w.model, w.x, w.ids, w.dy)
+    want = oracle_step(w.model, w.x, w.ids, w.dy)
+    assert_parity(got, want, BF16_TOL, f"{cfg} x{scale} {impl}")
+
+
+def _edge_module(d_in, d_out, ranks, dtype, seed=0, bias_std=0.1):
+    torch.manual_seed(seed)
+    m = MultiLoRALinear(d_in, d_out, ranks)
+    with torch.no_grad():
+        m.base.bias.normal_(0.0, bias_std)
+        for ad in m.adapters.values():
+            ad.B.normal_(0.0, 0.05)
+            ad.scaling = 1.5
+    return m.to(device=DEV, dtype=dtype)
+
+
+EDGE_CASES = {
+    # name: (d_in, d_out, ranks, ids builder)
+    "ragged_ranks": (256, 192, {0: 1, 1: 127, 2: 128, 3: 129, 4: 64},
+                     lambda: [0] * 1 + [1] * 130 + [2] * 5 + [3] * 77 + [4] * 200),
+    "empty_and_one_token": (128, 256, {0: 8, 1: 16, 2: 32, 3: 4},
+                            lambda: [1] * 1 + [3] * 300 + [2] * 1),
+    "many_segments_one_tile": (128, 128, {i: 1 + 7 * i for i in range(10)},
+                               lambda: sum(([i] * (3 + i) for i in range(10)), [])),
+    "unknown_ids": (128, 128, {0: 8, 5: 16}, lambda: [5] * 40 + [9] * 30 + [0] * 60 + [7] * 3),
+    "interleaved": (64, 64, {0: 2, 1: 4, 2: 8}, lambda: [0, 1, 2, 0, 2, 1, 0, 1, 2] * 31),
+    "tile_straddle": (192, 320, {0: 16, 1: 48, 2: 80}, lambda: [0] * 100 + [1] * 60 + [2] * 150 + [0] * 40),
+    "odd_shape": (200, 136, {0: 3, 1: 70}, lambda: [0] * 129 + [1] * 3),
+}
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("case", sorted(EDGE_CASES))
+def test_edge_cases(case, dtype):
+    d_in, d_out, ranks, idf = EDGE_CASES[case]
+    m = _edge_module(d_in, d_out, ranks, dtype)
+    ids = torch.tensor(idf(), dtype=torch.int64, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(ids.shape[0], d_in, generator=g, device=DEV).to(dtype)
+    dy = torch.randn(ids.shape[0], d_out, generator=g, device=DEV).to(dtype)
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert_parity(module_step(m, x, ids, dy), oracle_step(m, x, ids, dy), tol, case)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_delta_only(dtype):
+    """add_base=False: only the LoRA delta (the reference kernel's ADD_BASE=False)."""
+    m = _edge_module(256, 256, {0: 8, 1: 16, 2: 64}, dtype, bias_std=0.0)
+    ids = torch.tensor([0] * 100 + [1] * 200 + [2] * 37, device=DEV)
+    x = torch.randn(ids.shape[0], 256, device=DEV).to(dtype)
+    dy = torch.randn(ids.shape[0], 256, device=DEV).to(dtype)
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    got = module_step(m, x, ids, dy, add_base=False)
+    want = oracle_step(m, x, ids, dy, add_base=False)
+    assert_parity(got, want, tol, "delta-only")
+
+
+def test_tc_matches_simt_bf16():
+    """The two kernel families agree on the same bf16 inputs."""
+    w = workloads.build(workloads.spec("c1", 0.125), device=DEV)
+    w.model.impl = "tc"
+    a = module_step(w.model, w.x, w.ids, w.dy)
+    w.model.impl = "simt"
+    b = module_step(w.model, w.x, w.ids, w.dy)
+    for u, v in zip(a[:2], b[:2]):
+        assert orc.relative_l2(u, v) <= 1e-2
+
+
+def test_independent_adapter_forward():
+    torch.manual_seed(3)
+    ref = IndependentLoRALinear(64, 48, 8)
+    with torch.no_grad():
+        ref.adapter.B.normal_(0, 0.05)
+    ref = ref.to(DEV)
+    x = torch.randn(33, 64, device=DEV)
+    y = ref(x)
+    W, b = to_np(ref.base.weight), to_np(ref.base.bias)
+    ad = orc.OracleAdapter(to_np(ref.adapter.A), to_np(ref.adapter.B), ref.adapter.scaling)
+    want = to_np(x) @ W.T + b + orc.adapter_delta(to_np(x), ad)
+    assert orc.relative_l2(to_np(y), want) <= F32_TOL
+    d = ref.adapter(x)
+    assert orc.relative_l2(to_np(d), orc.adapter_delta(to_np(x), ad)) <= F32_TOL
+
+
+def test_no_device_error_word():
+    from tlora_b200 import _lib
+    assert _lib.device_error() == 0
