@@ -129,8 +129,9 @@ def cpu_baseline(w, target_s, steps=1):
             idx.extend(range(start, start + min(per, c)))
             start += c
         idx = np.asarray(idx)
-        x = w.x[torch.from_numpy(idx).to(w.x.device)].float().cpu().numpy()
-        dy = w.dy[torch.from_numpy(idx).to(w.x.device)].float().cpu().numpy()
+        sel = torch.from_numpy(idx).to(w.x.device)
+        x = w.x.detach()[sel].float().cpu().numpy()
+        dy = w.dy.detach()[sel].float().cpu().numpy()
         return x, ids_all[idx], dy
 
     def run(n_rows):

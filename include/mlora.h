@@ -102,6 +102,26 @@ int mlora_forward(const mlora_problem* prob, const mlora_routing* route,
                   void* Y, void* zsave, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* Stages of mlora_forward_staged. */
+#define MLORA_STAGE_SHRINK 1     /* write the low-rank intermediate of the tile range into zsave */
+#define MLORA_STAGE_MAIN 2       /* backbone + LoRA expand (+ bias) into the Y rows of the tile range */
+#define MLORA_STAGE_NO_EXPAND 4  /* with MAIN: leave the LoRA expand out (zsave is not read) */
+
+/* mlora_forward restricted to plan tiles [tile_begin, tile_end) (rows
+ * [128*tile_begin, min(128*tile_end, rows)) of X and Y; Y, X and zsave are
+ * the full-batch buffers) and to the given stages.  Used by the nano-batch
+ * pipeline (phase6_two_gpu_overlap.py:247-280): each nano-batch is a tile
+ * range, and a K-sharded rank other than the one that owns the LoRA expand
+ * runs MAIN | NO_EXPAND.  mlora_forward = SHRINK | MAIN over all tiles. */
+int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
+                         const void* X, const void* W, const void* bias,
+                         const void* A_pack, const void* B_pack,
+                         void* Y, void* zsave, void* workspace, size_t workspace_bytes,
+                         int32_t stages, int32_t tile_begin, int32_t tile_end, void* stream);
+
+/* Number of 128-row plan tiles of a problem (ceil(rows / 128)). */
+int32_t mlora_num_tiles(int64_t rows);
+
 /* Analytic backward.  Any of dX, dA_pack, dB_pack may be NULL to skip it.
  * W may be NULL: then dX holds only the LoRA term (delta-only forward).
  * dA_pack/dB_pack are written (not accumulated) for every adapter that owns at

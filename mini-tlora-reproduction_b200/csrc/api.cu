@@ -82,16 +82,29 @@ extern "C" int mlora_workspace_bytes(const mlora_problem* prob, const mlora_rout
   return MLORA_OK;
 }
 
-extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* route, const void* X,
-                             const void* W, const void* bias, const void* A_pack,
-                             const void* B_pack, void* Y, void* zsave, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+extern "C" int32_t mlora_num_tiles(int64_t rows) {
+  return rows <= 0 ? 0 : int32_t((rows + kTileRows - 1) / kTileRows);
+}
+
+extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
+                                    const void* X, const void* W, const void* bias,
+                                    const void* A_pack, const void* B_pack, void* Y, void* zsave,
+                                    void* workspace, size_t workspace_bytes, int32_t stages,
+                                    int32_t tile_begin, int32_t tile_end, void* stream) {
   thread_local Plan p;
   int st = build_plan(prob, route, &p);
   if (st != MLORA_OK) return st;
-  if (prob->rows == 0) return MLORA_OK;
-  if (!X || !Y || !workspace) return MLORA_ERR_INVALID_ARG;
-  if (!p.chunks.empty() && (!A_pack || !B_pack || !zsave)) return MLORA_ERR_INVALID_ARG;
+  if (stages & ~(MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN | MLORA_STAGE_NO_EXPAND)) return MLORA_ERR_INVALID_ARG;
+  if (tile_begin < 0 || tile_end < tile_begin || tile_end > p.n_tiles) return MLORA_ERR_INVALID_ARG;
+  if (prob->rows == 0 || tile_end == tile_begin) return MLORA_OK;
+  const bool need_z = !p.chunks.empty() &&
+                      ((stages & MLORA_STAGE_SHRINK) || ((stages & MLORA_STAGE_MAIN) && !(stages & MLORA_STAGE_NO_EXPAND)));
+  if (!X || !workspace) return MLORA_ERR_INVALID_ARG;
+  if ((stages & MLORA_STAGE_MAIN) && !Y) return MLORA_ERR_INVALID_ARG;
+  if (need_z && !zsave) return MLORA_ERR_INVALID_ARG;
+  if (!p.chunks.empty() && (stages & MLORA_STAGE_SHRINK) && !A_pack) return MLORA_ERR_INVALID_ARG;
+  if (need_z && (stages & MLORA_STAGE_MAIN) && !(stages & MLORA_STAGE_NO_EXPAND) && !B_pack)
+    return MLORA_ERR_INVALID_ARG;
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
   const int impl = choose_impl(prob);
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
@@ -106,6 +119,7 @@ extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* rou
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
     a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
     a.Y = Y; a.zsave = zsave;
+    a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
     return tc_forward(a, s);
   }
   SimtCall a;
@@ -116,7 +130,20 @@ extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* rou
   a.dtype = prob->dtype;
   a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
   a.Y = Y; a.zsave = zsave;
+  a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
+  a.c_begin = p.tile_chunk_begin[tile_begin];
+  a.c_end = p.tile_chunk_begin[tile_end];
   return simt_forward(a, s);
+}
+
+extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* route, const void* X,
+                             const void* W, const void* bias, const void* A_pack,
+                             const void* B_pack, void* Y, void* zsave, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!prob) return MLORA_ERR_INVALID_ARG;
+  return mlora_forward_staged(prob, route, X, W, bias, A_pack, B_pack, Y, zsave, workspace,
+                              workspace_bytes, MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN, 0,
+                              mlora_num_tiles(prob->rows), stream);
 }
 
 extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* route, const void* dY,

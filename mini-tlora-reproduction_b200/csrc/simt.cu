@@ -56,9 +56,9 @@ __device__ __forceinline__ void accum(float (&acc)[4][4], const FA& fa, const FB
 template <class T, bool BWD>
 __global__ void __launch_bounds__(NT) k_shrink(PlanDev plan, const T* __restrict__ src,
                                                 const T* __restrict__ pack, T* __restrict__ zt,
-                                                int64_t M, int d_in, int d_out, int R) {
+                                                int64_t M, int d_in, int d_out, int R, int c_begin) {
   __shared__ float As[BK][LD], Bs[BK][LD];
-  const int c = blockIdx.x, half = blockIdx.y;
+  const int c = c_begin + blockIdx.x, half = blockIdx.y;
   const Chunk ch = plan.chunks[c];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const int r0 = half * BM;
@@ -101,10 +101,10 @@ __global__ void __launch_bounds__(NT) k_main(PlanDev plan, const T* __restrict__
                                               const T* __restrict__ W, const T* __restrict__ bias,
                                               const T* __restrict__ pack, const T* __restrict__ zt,
                                               T* __restrict__ out, int64_t M, int d_in, int d_out,
-                                              int R) {
+                                              int R, int t0, int no_expand) {
   __shared__ float As[BK][LD], Bs[BK][LD];
   const int n0 = blockIdx.x * BN;
-  const int64_t m0 = int64_t(blockIdx.y) * BM;
+  const int64_t m0 = int64_t(t0) * kTileRows + int64_t(blockIdx.y) * BM;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const int N = BWD ? d_in : d_out;
   const int K = BWD ? d_out : d_in;
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(NT) k_main(PlanDev plan, const T* __restrict__
   }
   const int t = int(m0 / kTileRows);
   const int rt = int(m0 % kTileRows);
-  for (int c = plan.tile_chunk_begin[t]; c < plan.tile_chunk_begin[t + 1]; ++c) {
+  for (int c = plan.tile_chunk_begin[t]; !no_expand && c < plan.tile_chunk_begin[t + 1]; ++c) {
     const Chunk ch = plan.chunks[c];
     if (!(ch.lo < rt + BM && ch.hi > rt)) continue;  // rows of this half are zero
     const T* zc = zt + int64_t(c) * kTileRows * kChunk + int64_t(rt) * kChunk;
@@ -234,16 +234,19 @@ __global__ void k_sgd(SgdBatch batch, float lr) {
 
 template <class T>
 int launch_forward(const SimtCall& a, cudaStream_t st) {
-  if (a.n_chunks > 0) {
-    k_shrink<T, false><<<dim3(a.n_chunks, 2), NT, 0, st>>>(
-        a.plan, (const T*)a.X, (const T*)a.A_pack, (T*)a.zsave, a.M, a.d_in, a.d_out, a.R);
+  if ((a.stages & MLORA_STAGE_SHRINK) && a.c_end > a.c_begin) {
+    k_shrink<T, false><<<dim3(a.c_end - a.c_begin, 2), NT, 0, st>>>(
+        a.plan, (const T*)a.X, (const T*)a.A_pack, (T*)a.zsave, a.M, a.d_in, a.d_out, a.R, a.c_begin);
     count_launch();
   }
-  if (a.M > 0) {
-    dim3 grid((a.d_out + BN - 1) / BN, unsigned((a.M + BM - 1) / BM));
+  const int64_t r0 = int64_t(a.t0) * kTileRows;
+  const int64_t r1 = int64_t(a.t1) * kTileRows < a.M ? int64_t(a.t1) * kTileRows : a.M;
+  if ((a.stages & MLORA_STAGE_MAIN) && r1 > r0) {
+    dim3 grid((a.d_out + BN - 1) / BN, unsigned((r1 - r0 + BM - 1) / BM));
+    const int no_expand = (a.stages & MLORA_STAGE_NO_EXPAND) ? 1 : 0;
     k_main<T, false><<<grid, NT, 0, st>>>(a.plan, (const T*)a.X, (const T*)a.W, (const T*)a.bias,
                                           (const T*)a.B_pack, (const T*)a.zsave, (T*)a.Y, a.M,
-                                          a.d_in, a.d_out, a.R);
+                                          a.d_in, a.d_out, a.R, a.t0, no_expand);
     count_launch();
   }
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -253,14 +256,14 @@ template <class T>
 int launch_backward(const SimtCall& a, cudaStream_t st) {
   if (a.n_chunks > 0 && (a.dX || a.dA)) {
     k_shrink<T, true><<<dim3(a.n_chunks, 2), NT, 0, st>>>(
-        a.plan, (const T*)a.dY, (const T*)a.B_pack, (T*)a.dzt, a.M, a.d_in, a.d_out, a.R);
+        a.plan, (const T*)a.dY, (const T*)a.B_pack, (T*)a.dzt, a.M, a.d_in, a.d_out, a.R, 0);
     count_launch();
   }
   if (a.dX && a.M > 0) {
     dim3 grid((a.d_in + BN - 1) / BN, unsigned((a.M + BM - 1) / BM));
     k_main<T, true><<<grid, NT, 0, st>>>(a.plan, (const T*)a.dY, (const T*)a.W, nullptr,
                                          (const T*)a.A_pack, (const T*)a.dzt, (T*)a.dX, a.M,
-                                         a.d_in, a.d_out, a.R);
+                                         a.d_in, a.d_out, a.R, 0, 0);
     count_launch();
   }
   if (a.n_reduce > 0 && (a.dA || a.dB)) {

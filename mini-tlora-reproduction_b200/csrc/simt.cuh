@@ -17,6 +17,9 @@ struct SimtCall {
   void* zsave = nullptr;  // Zt (fwd output, bwd input)
   void* dzt = nullptr;    // dZt scratch (bwd)
   void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+  // forward stages (MLORA_STAGE_*), plan tile range [t0, t1) and its chunk range
+  int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
+  int t0 = 0, t1 = 0, c_begin = 0, c_end = 0;
 };
 
 int simt_forward(const SimtCall& a, cudaStream_t st);

@@ -29,6 +29,8 @@
 // word, lets in-flight copies and MMAs land, frees TMEM and returns.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "tc.cuh"
 
 namespace mlora {
@@ -54,6 +56,10 @@ struct TcParams {
   int64_t M;
   int d_in, d_out, R;
   int n_items;
+  int item0;        // shrink: first shrink item of the launch
+  int tile0;        // main: first plan tile of the launch
+  int n_tiles_rng;  // main: plan tiles of the launch
+  int no_expand;    // main: leave the LoRA expand out
   int n_nblk;   // main modes: 256-wide N blocks
   int nk_main;  // main / shrink: 64-wide K blocks of the dense part
   const __nv_bfloat16* bias;
@@ -183,16 +189,16 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item) {
     const int per_group = kGroupM * p.n_nblk;
     const int g = item / per_group, r = item % per_group;
     const int t0 = g * kGroupM;
-    const int gs = min(kGroupM, p.plan.n_tiles - t0);
+    const int gs = min(kGroupM, p.n_tiles_rng - t0);
     it.nb = r / gs;
-    it.t = t0 + r % gs;
+    it.t = p.tile0 + t0 + r % gs;
     it.c0 = p.plan.tile_chunk_begin[it.t];
-    it.nc = p.plan.tile_chunk_begin[it.t + 1] - it.c0;
+    it.nc = p.no_expand ? 0 : p.plan.tile_chunk_begin[it.t + 1] - it.c0;
     it.nk1 = p.nk_main;
     it.nk = it.nk1 + it.nc;
     it.n = kAccCols;
   } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
-    const ShrinkItem s = p.plan.shrink[item];
+    const ShrinkItem s = p.plan.shrink[p.item0 + item];
     it.t = s.tile;
     it.c0 = s.c0;
     it.nc = s.nc;
@@ -543,24 +549,35 @@ bool tc_available() {
 int tc_forward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
   const int64_t zrows = int64_t(n_chunks) * 128;
-  if (n_chunks > 0) {
+  if (a.t1 <= a.t0) return MLORA_OK;
+  if (n_chunks > 0 && (a.stages & MLORA_STAGE_SHRINK)) {
+    // shrink items are in tile order: the launch covers those of [t0, t1)
+    const std::vector<ShrinkItem>& sh = a.host->shrink;
+    auto lo = std::lower_bound(sh.begin(), sh.end(), a.t0, [](const ShrinkItem& s, int t) { return s.tile < t; });
+    auto hi = std::lower_bound(sh.begin(), sh.end(), a.t1, [](const ShrinkItem& s, int t) { return s.tile < t; });
     TcParams prm = base_params(a);
     if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || !make_map(&prm.mB0, a.A_pack, a.R, a.d_in, 64))
       return MLORA_ERR_UNSUPPORTED;
-    prm.n_items = a.plan.n_shrink;
+    prm.item0 = int(lo - sh.begin());
+    prm.n_items = int(hi - lo);
     prm.nk_main = (a.d_in + 63) / 64;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
     int s = launch<SHRINK_FWD>(prm, st);
     if (s != MLORA_OK) return s;
   }
+  if (!(a.stages & MLORA_STAGE_MAIN)) return MLORA_OK;
+  const bool expand = n_chunks > 0 && !(a.stages & MLORA_STAGE_NO_EXPAND);
   TcParams prm = base_params(a);
   if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, 256)))
     return MLORA_ERR_UNSUPPORTED;
-  if (n_chunks > 0 &&
+  if (expand &&
       (!make_map(&prm.mA1, a.zsave, zrows, 64, 128) || !make_map(&prm.mB1, a.B_pack, a.d_out, a.R, 256)))
     return MLORA_ERR_UNSUPPORTED;
+  prm.no_expand = expand ? 0 : 1;
+  prm.tile0 = a.t0;
+  prm.n_tiles_rng = a.t1 - a.t0;
   prm.n_nblk = (a.d_out + 255) / 256;
-  prm.n_items = a.plan.n_tiles * prm.n_nblk;
+  prm.n_items = prm.n_tiles_rng * prm.n_nblk;
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
@@ -587,6 +604,8 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     if (n_chunks > 0 &&
         (!make_map(&prm.mA1, a.dzt, zrows, 64, 128) || !make_map(&prm.mB1, a.A_pack, a.R, a.d_in, 64)))
       return MLORA_ERR_UNSUPPORTED;
+    prm.tile0 = 0;
+    prm.n_tiles_rng = a.plan.n_tiles;
     prm.n_nblk = (a.d_in + 255) / 256;
     prm.n_items = a.plan.n_tiles * prm.n_nblk;
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;

@@ -17,6 +17,9 @@ struct TcCall {
   void* zsave = nullptr;
   void* dzt = nullptr;
   void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+  // forward stages (MLORA_STAGE_*) and plan tile range [t0, t1)
+  int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
+  int t0 = 0, t1 = 0;
 };
 
 // true when the driver exposes cuTensorMapEncodeTiled and the current device

@@ -31,6 +31,10 @@ BF16 = 1
 RANK_CHUNK = 64
 TILE_ROWS = 128
 
+STAGE_SHRINK = 1
+STAGE_MAIN = 2
+STAGE_NO_EXPAND = 4
+
 IMPL_AUTO = 0
 IMPL_SIMT = 1
 IMPL_TC = 2
@@ -80,6 +84,10 @@ SIGNATURES = {
     "mlora_workspace_bytes": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), ctypes.POINTER(ctypes.c_size_t)]),
     "mlora_forward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,
                                      _VP, _VP, _VP, ctypes.c_size_t, _VP]),
+    "mlora_forward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,
+                                            _VP, _VP, _VP, _VP, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, _VP]),
+    "mlora_num_tiles": (ctypes.c_int32, [ctypes.c_int64]),
     "mlora_backward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,
                                       _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _VP]),
     "mlora_sgd": (ctypes.c_int, [ctypes.POINTER(SgdItem), ctypes.c_int32, ctypes.c_float, ctypes.c_int32, _VP]),

@@ -134,16 +134,23 @@ def route(ids: torch.Tensor, table: AdapterTable, device: torch.device) -> Route
     if rows == 0:
         return RoutePlan(0, np.zeros(1, np.int32), np.zeros(0, np.int32), None, np.zeros(n, bool))
     if ids.device.type != "cuda":
-        # host ids: routing is host logic on an O(rows) integer array
+        # host ids: routing is host logic on an O(rows) integer array.  Fast
+        # path: runs of equal raw id (one vectorised pass), mapped to slots.
         slot_of = table.slot_of()
-        v = ids.detach().cpu().numpy().astype(np.int64)
+        v = ids.detach().numpy().astype(np.int64, copy=False)
+        head = np.empty(rows, dtype=bool)
+        head[0] = True
+        np.not_equal(v[1:], v[:-1], out=head[1:])
+        starts = np.flatnonzero(head)
+        if len(starts) <= max(64, 2 * n + 2, rows // TILE_ROWS + 1):
+            rs = np.array([slot_of.get(int(a), -1) for a in v[starts]], dtype=np.int32)
+            keep = np.ones(len(rs), dtype=bool)
+            keep[1:] = rs[1:] != rs[:-1]  # adjacent runs that map to one slot merge
+            starts, rs = starts[keep], rs[keep]
+            if _use_runs(len(starts), rs, rows):
+                return _segments_from_runs(starts, rs, rows, n)
         uniq, inv = np.unique(v, return_inverse=True)
         slots = np.array([slot_of.get(int(u), -1) for u in uniq], dtype=np.int32)[inv]
-        head = np.ones(rows, dtype=bool)
-        head[1:] = slots[1:] != slots[:-1]
-        starts = np.nonzero(head)[0]
-        if _use_runs(len(starts), slots[starts], rows):
-            return _segments_from_runs(starts, slots[starts], rows, n)
         key = np.where(slots < 0, n, slots)
         order = np.argsort(key, kind="stable").astype(np.int32)
         counts = np.bincount(key, minlength=n + 1)
@@ -245,6 +252,39 @@ def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     if st.plan.perm is not None:
         y = scatter_rows(y, st.plan.perm)
     return y, z, xs, args
+
+
+class StagedForward:
+    """Forward of one routing plan split into stages and tile ranges (the
+    nano-batch pipeline): ``shrink(t0, t1)`` writes the low-rank
+    intermediate of tiles [t0, t1) into ``z``; ``main(t0, t1, expand)``
+    writes rows [128 t0, 128 t1) of ``y`` (backbone + bias, + LoRA expand when
+    ``expand``)."""
+
+    def __init__(self, x, W, bias, st: LayerState, y=None):
+        self.x, self.W, self.bias, self.st = x, W, bias, st
+        rows, d_in = x.shape
+        d_out = st.B_pack.shape[0]
+        self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling)
+        zb, wb = self.args.sizes()
+        dev = x.device
+        self.y = y if y is not None else torch.empty(rows, d_out, dtype=x.dtype, device=dev)
+        self.z = torch.empty(max(zb, 1), dtype=torch.uint8, device=dev)
+        self.ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+        self.wb = wb
+        self.n_tiles = int(_lib.lib().mlora_num_tiles(rows))
+
+    def _run(self, stages, t0, t1, bias):
+        _lib.call("mlora_forward_staged", ctypes.byref(self.args.prob), ctypes.byref(self.args.route),
+                  _ptr(self.x), _ptr(self.W), _ptr(bias), _ptr(self.st.A_pack), _ptr(self.st.B_pack),
+                  _ptr(self.y), _ptr(self.z), _ptr(self.ws), self.wb, stages, t0, t1, _stream(self.x.device))
+
+    def shrink(self, t0=0, t1=None):
+        self._run(_lib.STAGE_SHRINK, t0, self.n_tiles if t1 is None else t1, None)
+
+    def main(self, t0=0, t1=None, expand=True, add_bias=True):
+        stages = _lib.STAGE_MAIN | (0 if expand else _lib.STAGE_NO_EXPAND)
+        self._run(stages, t0, self.n_tiles if t1 is None else t1, self.bias if add_bias else None)
 
 
 def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, want_dB: bool):

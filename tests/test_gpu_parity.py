@@ -5,7 +5,6 @@ Tolerances (north star): relative L2 <= 1e-5 in fp32 mode, <= 2e-2 in bf16
 mode (fp32 accumulation), for Y, dX, dA, dB and the one-step SGD update.
 """
 
-import copy
 import os
 
 import numpy as np
@@ -47,12 +46,16 @@ def test_golden_fp32(golden_dir, name, ids_on):
     """The reference's own cases (tests/test_equivalence.py shapes and seeds),
     fp32, against the reference's outputs."""
     z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    def fwd_bwd(m):
+        x = torch.from_numpy(z["x"]).to(DEV).requires_grad_(True)
+        ids = torch.from_numpy(z["ids"]).to(ids_on)
+        y = m(x, ids)
+        loss = torch.nn.functional.mse_loss(y, torch.from_numpy(z["target"]).to(DEV), reduction="sum")
+        loss.backward()
+        return x, y
+
     m = _golden_module(z)
-    x = torch.from_numpy(z["x"]).to(DEV).requires_grad_(True)
-    ids = torch.from_numpy(z["ids"]).to(ids_on)
-    y = m(x, ids)
-    loss = torch.nn.functional.mse_loss(y, torch.from_numpy(z["target"]).to(DEV), reduction="sum")
-    loss.backward()
+    x, y = fwd_bwd(m)
     assert orc.relative_l2(to_np(y), z["Y"]) <= F32_TOL
     assert orc.relative_l2(to_np(x.grad), z["dX"]) <= F32_TOL
     for a in z["adapter_ids"]:
@@ -66,7 +69,8 @@ def test_golden_fp32(golden_dir, name, ids_on):
     # isolated SGD with the reference's optimizer usage and with the fused step
     lr = float(z["lr"])
     opt_ids = [int(a) for a in z["opt_ids"]]
-    m2 = copy.deepcopy(m)
+    m2 = _golden_module(z)  # same inputs through a second module for the fused step
+    fwd_bwd(m2)
     opts = [torch.optim.SGD(m.adapter_parameters(a), lr=lr) for a in opt_ids]
     for o in opts:
         o.step()

@@ -1,0 +1,164 @@
+"""World-size-2 gloo tests (CPU) of the K-sharded nano-batch pipeline: the
+sharding, the per-nano-batch all-reduce choreography and the rank-0-only
+bias / LoRA expand must reproduce the unsharded layer (the oracle).  The
+native kernels are replaced by a dense torch stand-in with the same stage
+semantics; the kernels themselves are covered by the GPU parity tests."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import mlora_oracle as orc
+from tlora_b200 import MultiLoRALinear
+from tlora_b200.overlap import ShardedLayer, shard_columns
+from tlora_b200.nano import split_ranges
+from tlora_b200 import ops
+
+TILE = 128
+
+
+class DenseCompute:
+    """Stage-for-stage dense stand-in of NativeCompute (fp64 on CPU)."""
+
+    def _rowmask(self, layer, plan, rows):
+        # per-row scale on the packed rank columns of the row's adapter
+        R = layer.table.r_pack
+        m = torch.zeros(rows, R, dtype=torch.float64)
+        for s in range(plan.n_seg):
+            a = int(plan.seg_adapter[s])
+            if a < 0:
+                continue
+            o, r = int(layer.table.pack_off[a]), int(layer.table.rank[a])
+            m[plan.seg_start[s]:plan.seg_start[s + 1], o:o + r] = float(layer.scaling[a])
+        return m
+
+    def begin(self, layer, x_p, plan):
+        rows = x_p.shape[0]
+        return {"x": x_p, "plan": plan, "mask": self._rowmask(layer, plan, rows),
+                "z": torch.zeros(rows, layer.table.r_pack, dtype=torch.float64),
+                "y": torch.zeros(rows, layer.B_pack.shape[0], dtype=torch.float64),
+                "n_tiles": (rows + TILE - 1) // TILE, "layer": layer}
+
+    def shrink(self, ctx):
+        L = ctx["layer"]
+        ctx["z"].copy_((ctx["x"] @ L.A_pack.T) * ctx["mask"])
+
+    def main(self, ctx, t0, t1, expand, add_bias):
+        L = ctx["layer"]
+        r0, r1 = t0 * TILE, min(t1 * TILE, ctx["x"].shape[0])
+        v = ctx["x"][r0:r1] @ L.W.T
+        if expand:
+            v = v + ctx["z"][r0:r1] @ L.B_pack.T
+        if add_bias and L.bias is not None:
+            v = v + L.bias
+        ctx["y"][r0:r1] = v
+
+    def backward(self, ctx, layer, x_p, dy):
+        dz = (dy @ layer.B_pack) * ctx["mask"]
+        dx = dy @ layer.W + dz @ layer.A_pack
+        return dx, dz.T @ x_p, dy.T @ ctx["z"]
+
+    def sgd(self, layer, plan, dA, dB, lr):
+        for i in range(layer.table.n):
+            if plan.active[i]:
+                o, r = int(layer.table.pack_off[i]), int(layer.table.rank[i])
+                layer.A_pack[o:o + r] -= lr * dA[o:o + r]
+                layer.B_pack[:, o:o + r] -= lr * dB[:, o:o + r]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _build(seed=0):
+    torch.manual_seed(seed)
+    m = MultiLoRALinear(256, 96, {0: 4, 1: 70, 2: 8}).double()
+    with torch.no_grad():
+        m.base.bias.normal_(0, 0.1)
+        for ad in m.adapters.values():
+            ad.B.normal_(0, 0.05)
+            ad.scaling = 2.0
+    ids = torch.tensor([0] * 150 + [1] * 100 + [2] * 77 + [9] * 5)
+    g = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(ids.shape[0], 256, generator=g, dtype=torch.float64)
+    dy = torch.randn(ids.shape[0], 96, generator=g, dtype=torch.float64)
+    return m, ids, x, dy
+
+
+def _worker(rank, world, port, n_nano, pipelined, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, ids, x, dy = _build()
+        layer = ShardedLayer(m, rank, world, compute=DenseCompute())
+        plan = ops.route(ids, layer.table, torch.device("cpu"))
+        x_p = layer.shard_input(x)
+        y, dx_p = layer.step(x_p, plan, dy, n_nano, lr=0.01, pipelined=pipelined)
+        sizes = [shard_columns(256, r, world) for r in range(world)]
+        parts = [torch.zeros(x.shape[0], e - s, dtype=torch.float64) for s, e in sizes]
+        dist.all_gather(parts, dx_p.contiguous())
+        a_parts = [torch.zeros(layer.A_pack.shape[0], e - s, dtype=torch.float64) for s, e in sizes]
+        dist.all_gather(a_parts, layer.A_pack.contiguous())
+        if rank == 0:
+            q.put({"y": y.numpy().copy(), "dx": torch.cat(parts, 1).numpy(),
+                   "A_pack": torch.cat(a_parts, 1).numpy(), "B_pack": layer.B_pack.numpy().copy(),
+                   "pack_off": layer.table.pack_off.copy(), "rank": layer.table.rank.copy()})
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n_nano,pipelined", [(1, True), (3, True), (2, False), (16, True)])
+def test_sharded_step_matches_unsharded(n_nano, pipelined):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, pipelined, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+
+    m, ids, x, dy = _build()
+    W = m.base.weight.detach().numpy()
+    b = m.base.bias.detach().numpy()
+    ads = {int(k): orc.OracleAdapter(a.A.detach().numpy(), a.B.detach().numpy(), float(a.scaling))
+           for k, a in m.adapters.items()}
+    xn, idn, dyn = x.numpy(), ids.numpy(), dy.numpy()
+    Y = orc.multi_lora_forward(xn, idn, W, b, ads)
+    dX, dA, dB = orc.multi_lora_backward(xn, idn, W, ads, dyn)
+    assert orc.relative_l2(res["y"], Y) < 1e-12
+    assert orc.relative_l2(res["dx"], dX) < 1e-12
+    for i, a in enumerate(sorted(ads)):
+        o, r = int(res["pack_off"][i]), int(res["rank"][i])
+        A_next = orc.sgd_step(ads[a].A, dA[a], 0.01)
+        B_next = orc.sgd_step(ads[a].B, dB[a], 0.01)
+        assert orc.relative_l2(res["A_pack"][o:o + r], A_next) < 1e-12
+        assert orc.relative_l2(res["B_pack"][:, o:o + r], B_next) < 1e-12
+
+
+def test_shard_columns_cover_exactly():
+    for d in [64, 192, 4096, 8192, 11008]:
+        for world in [1, 2, 4, 8]:
+            spans = [shard_columns(d, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == d
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert all(s % 64 == 0 for s, _ in spans)
+
+
+def test_nano_ranges_over_tiles():
+    for tiles in [1, 3, 512]:
+        for n in [1, 2, 4, 8, 16, 32]:
+            r = split_ranges(tiles, n)
+            assert r[0][0] == 0 and r[-1][1] == tiles and len(r) == min(n, tiles)
