@@ -122,6 +122,29 @@ int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
 /* Number of 128-row plan tiles of a problem (ceil(rows / 128)). */
 int32_t mlora_num_tiles(int64_t rows);
 
+/* Fused forward for callers that cannot allocate device memory (no
+ * counterpart in the reference, which always allocates through PyTorch).
+ * Serving runtimes and plugin hosts that reserve all device memory up front,
+ * and C/Go/Java hosts with no device allocator of their own, cannot hand this
+ * library a cudaMalloc'd workspace; this call takes only the inputs and Y and
+ * computes what mlora_forward computes, keeping its scratch (plan tables and
+ * the low-rank intermediate) in a fixed 32 MiB array of device memory that the
+ * library holds on every GPU that loads it until the process exits.
+ *  - A problem whose scratch does not fit in 32 MiB returns
+ *    MLORA_ERR_WORKSPACE and launches nothing.
+ *  - The first call on each device looks the array's address up
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture on the device.
+ *  - All calls on a device share the array and it keeps the last call's
+ *    contents; each call writes all the scratch it reads, but calls that
+ *    overlap on the GPU (several streams or host threads at once) race and
+ *    must be serialised by the caller.
+ *  - The intermediate is not returned, so there is no backward for this call.
+ *  - Calls no cudaMalloc, cudaFree or allocating library routine. */
+int mlora_forward_noalloc(const mlora_problem* prob, const mlora_routing* route,
+                          const void* X, const void* W, const void* bias,
+                          const void* A_pack, const void* B_pack, void* Y, void* stream);
+
 /* Analytic backward.  Any of dX, dA_pack, dB_pack may be NULL to skip it.
  * W may be NULL: then dX holds only the LoRA term (delta-only forward).
  * dA_pack/dB_pack are written (not accumulated) for every adapter that owns at

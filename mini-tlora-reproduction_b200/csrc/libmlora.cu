@@ -7,3 +7,4 @@
 #include "route.cu"
 #include "tc.cu"
 #include "api.cu"
+#include "noalloc.cu"

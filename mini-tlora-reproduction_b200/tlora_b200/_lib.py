@@ -88,6 +88,8 @@ SIGNATURES = {
                                             _VP, _VP, _VP, _VP, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, _VP]),
     "mlora_num_tiles": (ctypes.c_int32, [ctypes.c_int64]),
+    "mlora_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,
+                                             _VP, _VP, _VP]),
     "mlora_backward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,
                                       _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _VP]),
     "mlora_sgd": (ctypes.c_int, [ctypes.POINTER(SgdItem), ctypes.c_int32, ctypes.c_float, ctypes.c_int32, _VP]),
