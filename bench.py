@@ -36,11 +36,14 @@ UNIT = "tokens/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernels", default="auto", choices=["auto", "tc", "tc1", "simt"],
+                   help="kernel family of the module (tc = 2-SM pair mainloops, tc1 = 1-SM)")
+    p.add_argument("--no-cublas", action="store_true", help="skip the cuBLAS backbone-GEMM context measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU time of the baseline sample")
     return p.parse_args()
 
@@ -69,7 +72,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -163,6 +166,29 @@ def train_step(m, x, ids, dy, lr, plan=None):
     return y
 
 
+def cublas_backbone(w, dev, reps=10):
+    """Context only: cuBLAS (torch.matmul) on the backbone GEMM shapes of the
+    step, Y = X W^T and dX = dY W, without the LoRA terms."""
+    W = w.model.base.weight.detach()
+    x = w.x.detach()
+    dy = w.dy.detach()
+    out = {}
+    for name, fn, flops in (("fwd", lambda: torch.matmul(x, W.t()), 2.0 * x.shape[0] * W.shape[0] * W.shape[1]),
+                            ("dx", lambda: torch.matmul(dy, W), 2.0 * x.shape[0] * W.shape[0] * W.shape[1])):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / reps
+        out[name] = {"ms": round(t, 4), "tflops": round(flops / (t / 1000.0) / 1e12, 1)}
+    return out
+
+
 def run_single(args, peaks_d, peaks_kind):
     from tlora_b200 import _lib, workloads
 
@@ -171,6 +197,7 @@ def run_single(args, peaks_d, peaks_kind):
     sp = workloads.spec(args.workload)
     w = workloads.build(sp, device=dev)
     m = w.model
+    m.impl = args.kernels
     x = w.x.requires_grad_(True)
     lr = sp.lr
     step_fn = (lambda: train_step(m, x, w.ids, w.dy, lr)) if sp.train else (lambda: m(x, w.ids))
@@ -228,6 +255,8 @@ def run_single(args, peaks_d, peaks_kind):
         e2e_step()
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / n_e2e
 
+    cublas = None if args.no_cublas else cublas_backbone(w, dev)
+
     rows = sp.rows
     tokens_s = rows / (ms / 1000.0)
     # roofline: the dominant tensor-core kernel is the fused forward mainloop
@@ -267,6 +296,7 @@ def run_single(args, peaks_d, peaks_kind):
                 "d2h_bytes_per_step": int(probe.numel() * probe.element_size())},
         "gpu_launches": int(launches),
         "clocks": ck,
+        "cublas_backbone": cublas,
     }
     if not args.no_cpu_baseline:
         tps, cores, smp = cpu_baseline(w, args.cpu_seconds)

@@ -59,12 +59,13 @@ extern "C" {
 /* adapter ranks are packed in chunks of this many rows/columns */
 #define MLORA_RANK_CHUNK 64
 /* rows per tile of the routing plan */
-#define MLORA_TILE_ROWS 128
+#define MLORA_TILE_ROWS 256
 
 /* kernel family selection for mlora_forward / mlora_backward */
 #define MLORA_IMPL_AUTO 0   /* tcgen05 tensor-core kernels when the shape allows, else SIMT */
 #define MLORA_IMPL_SIMT 1   /* CUDA-core kernels, fp32 accumulate (exact fp32 mode) */
-#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only) */
+#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only); mainloops on 2-SM pairs */
+#define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with single-SM mainloops (comparison path) */
 
 typedef struct mlora_problem {
   int64_t rows;   /* M: rows of X in this call */
@@ -72,6 +73,10 @@ typedef struct mlora_problem {
   int32_t d_out;  /* out_features (N of the backbone GEMM) */
   int32_t dtype;  /* MLORA_F32 or MLORA_BF16, for every tensor argument */
   int32_t impl;   /* MLORA_IMPL_* */
+  int32_t max_ctas; /* cap on the resident CTAs of the persistent tensor-core kernels;
+                       0 = one per SM.  A smaller value leaves SMs free for
+                       communication kernels running at the same time (the
+                       nano-batch all-reduce overlap). */
 } mlora_problem;
 
 typedef struct mlora_routing {

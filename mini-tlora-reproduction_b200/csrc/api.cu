@@ -54,7 +54,8 @@ bool tc_shape_ok(const mlora_problem* prob) {
 
 int choose_impl(const mlora_problem* prob) {
   if (prob->impl == MLORA_IMPL_SIMT) return MLORA_IMPL_SIMT;
-  if (prob->impl == MLORA_IMPL_TC) return tc_shape_ok(prob) ? MLORA_IMPL_TC : -1;
+  if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM)
+    return tc_shape_ok(prob) ? MLORA_IMPL_TC : -1;
   if (prob->impl != MLORA_IMPL_AUTO) return -1;
   return (tc_shape_ok(prob) && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
 }
@@ -120,6 +121,8 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
     a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
     a.Y = Y; a.zsave = zsave;
     a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
+    a.max_ctas = prob->max_ctas;
+    a.pair_mma = prob->impl != MLORA_IMPL_TC_1SM;
     return tc_forward(a, s);
   }
   SimtCall a;
@@ -172,6 +175,8 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
     a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
     a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+    a.max_ctas = prob->max_ctas;
+    a.pair_mma = prob->impl != MLORA_IMPL_TC_1SM;
     return tc_backward(a, s);
   }
   SimtCall a;

@@ -235,7 +235,7 @@ __global__ void k_sgd(SgdBatch batch, float lr) {
 template <class T>
 int launch_forward(const SimtCall& a, cudaStream_t st) {
   if ((a.stages & MLORA_STAGE_SHRINK) && a.c_end > a.c_begin) {
-    k_shrink<T, false><<<dim3(a.c_end - a.c_begin, 2), NT, 0, st>>>(
+    k_shrink<T, false><<<dim3(a.c_end - a.c_begin, kTileRows / BM), NT, 0, st>>>(
         a.plan, (const T*)a.X, (const T*)a.A_pack, (T*)a.zsave, a.M, a.d_in, a.d_out, a.R, a.c_begin);
     count_launch();
   }
@@ -255,7 +255,7 @@ int launch_forward(const SimtCall& a, cudaStream_t st) {
 template <class T>
 int launch_backward(const SimtCall& a, cudaStream_t st) {
   if (a.n_chunks > 0 && (a.dX || a.dA)) {
-    k_shrink<T, true><<<dim3(a.n_chunks, 2), NT, 0, st>>>(
+    k_shrink<T, true><<<dim3(a.n_chunks, kTileRows / BM), NT, 0, st>>>(
         a.plan, (const T*)a.dY, (const T*)a.B_pack, (T*)a.dzt, a.M, a.d_in, a.d_out, a.R, 0);
     count_launch();
   }

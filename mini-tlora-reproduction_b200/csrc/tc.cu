@@ -1,6 +1,6 @@
 // tcgen05 / TMEM kernel family of the multi-LoRA linear (sm_100a).
 //
-// One persistent, warp-specialised kernel template serves five roles:
+// Five roles over the routing plan (256-row tiles, 64-column rank chunks):
 //
 //   FWD_MAIN    Y  = X W^T + bias + sum_c Zt[c] Bpack[:, chunk c]^T
 //   DX_MAIN     dX = dY W       + sum_c dZt[c] Apack[chunk c, :]
@@ -8,22 +8,34 @@
 //   SHRINK_BWD  dZt[c] = rowmask_c(s_a dY_tile Bpack[:, chunk c])
 //   REDUCE      dA chunk = sum_tiles dZt[c]^T X_tile,  dB chunk = sum_tiles dY_tile^T Zt[c]
 //
-// The LoRA expand is not a separate pass: each 128-row tile's low-rank
-// blocks Zt[c] (64 rank columns, zero outside the tile rows of the block's
-// segment) are extra K-blocks of the backbone mainloop, accumulated into the
-// same TMEM accumulator, so the full delta-W is never formed and Y is
-// written once.  This replaces the reference's per-row CUDA-core kernel
+// The LoRA expand is not a separate pass: each tile's low-rank blocks Zt[c]
+// (64 rank columns, zero outside the tile rows of the block's segment) are
+// extra K-blocks of the backbone mainloop, accumulated into the same TMEM
+// accumulator, so the full delta-W is never formed and Y is written once.
+// This replaces the reference's per-row CUDA-core kernel
 // (fused_lora_residual_kernel, phase5c_fused_triton.py:201-300) plus the
 // separate cuBLAS backbone (phase5c_fused_triton.py:555) and the per-adapter
 // PyTorch backward (phase5d_triton_training.py:248-325).
 //
-// Warp roles (192 threads): warp 0 lane 0 issues TMA loads into a 4-stage
-// shared-memory ring; warp 1 owns TMEM (512 columns = two 128x256 fp32
-// accumulators) and lane 0 issues tcgen05.mma; warps 2..5 drain the
-// accumulator of the previous work item (tcgen05.ld) while the next one
-// accumulates.  All operand tiles are 64 bf16 (128 B) wide with the 128-byte
-// swizzle; K-major operands are 128/256-row boxes, MN-major operands are
-// stacks of 64x64 boxes.  No TMA load here uses cluster multicast.
+// Two kernel templates, both persistent and warp-specialised (192 threads:
+// warp 0 lane 0 issues TMA loads into a shared-memory ring, warp 1 owns TMEM
+// (512 columns = two 128x256 fp32 accumulators) and lane 0 issues
+// tcgen05.mma, warps 2..5 drain the previous work item's accumulator with
+// tcgen05.ld while the next one accumulates):
+//
+//  * k_tc2 (FWD_MAIN, DX_MAIN): a cluster of two CTAs on two SMs computes a
+//    256x256 tile with tcgen05.mma.cta_group::2 (M = 256, N = 256).  Each CTA
+//    stages its own 128 rows of A and its own 128-row half of B (32 KB per
+//    stage, 6 stages); the TMA loads of both CTAs complete on the even CTA's
+//    barrier, the even CTA issues the MMAs and its commits signal the barriers
+//    of both CTAs.  Per SM this moves 2/3 of the operand bytes of a 1-SM
+//    128x256 tile for the same MMA work.
+//  * k_tc (SHRINK_*, REDUCE, and the 1-SM variant of the mainloops): one CTA,
+//    M = 128, N <= 256, 4 stages of 48 KB.
+//
+// All operand tiles are 64 bf16 (128 B) wide with the 128-byte swizzle;
+// K-major operands are 128/256-row boxes, MN-major operands are stacks of
+// 64x64 boxes.  No TMA load here uses cluster multicast.
 //
 // Every mbarrier wait is bounded: on timeout the kernel sets the device error
 // word, lets in-flight copies and MMAs land, frees TMEM and returns.
@@ -36,17 +48,23 @@
 namespace mlora {
 namespace {
 
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
-constexpr int kABytes = 128 * 64 * 2;  // 16 KB
-constexpr int kBBytes = 256 * 64 * 2;  // 32 KB
-constexpr int kBox64 = 64 * 64 * 2;    // 8 KB
-constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kBox64 = 64 * 64 * 2;  // one 64x64 bf16 box, 8 KB
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;
-constexpr int kGroupM = 16;
+constexpr int kGroupM = 8;           // raster group, in 256-row tiles
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kHalfRows = 128;       // rows of one CTA's A tile = TMEM lanes
+// 1-SM kernel: A 128x64 (16 KB) + B up to 256x64 (32 KB) per stage
+constexpr int kStages1 = 4;
+constexpr int kA1Bytes = 128 * 64 * 2;
+constexpr int kStage1Bytes = kA1Bytes + 256 * 64 * 2;
+constexpr int kSmem1 = kStages1 * kStage1Bytes + 1024 + 256;
+// 2-SM kernel: per CTA A 128x64 (16 KB) + B half 128x64 (16 KB) per stage
+constexpr int kStages2 = 6;
+constexpr int kA2Bytes = 128 * 64 * 2;
+constexpr int kStage2Bytes = kA2Bytes + 128 * 64 * 2;
+constexpr int kSmem2 = kStages2 * kStage2Bytes + 1024 + 256;
 
 enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
 
@@ -60,8 +78,8 @@ struct TcParams {
   int tile0;        // main: first plan tile of the launch
   int n_tiles_rng;  // main: plan tiles of the launch
   int no_expand;    // main: leave the LoRA expand out
-  int n_nblk;   // main modes: 256-wide N blocks
-  int nk_main;  // main / shrink: 64-wide K blocks of the dense part
+  int n_nblk;       // main: 256-wide N blocks
+  int nk_main;      // main / shrink: 64-wide K blocks of the dense part
   const __nv_bfloat16* bias;
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
   __nv_bfloat16* dA;
@@ -76,6 +94,20 @@ __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count));
@@ -116,11 +148,24 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+// arrive on a barrier given by its shared::cluster address (own or peer CTA)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
 __device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           su32(dst)),
       "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// Load into this CTA's shared memory, completing on the barrier at the
+// shared::cluster address `bar` (the even CTA's barrier of the pair).
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          su32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
@@ -136,8 +181,27 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+__device__ __forceinline__ void tc_mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
 __device__ __forceinline__ void tc_commit(uint64_t* b) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
+               : "memory");
+}
+// commit of the pair's MMAs, arriving on the barrier at this offset in both CTAs
+__device__ __forceinline__ void tc_commit_pair_both(uint64_t* b) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          su32(b)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_local(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
                : "memory");
 }
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -160,46 +224,67 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) |
          (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
-// Instruction descriptor: bf16 x bf16 -> fp32, M = 128, N = n.
-__device__ __forceinline__ uint32_t idesc_bf16(int n, bool a_mn, bool b_mn) {
+// Instruction descriptor: bf16 x bf16 -> fp32, M = m, N = n.
+__device__ __forceinline__ uint32_t idesc_bf16(int m, int n, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
-         (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float (&f)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                       pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+}
 
 // ------------------------------------------------------------------ items
 struct Item {
   int nk, nk1, n;  // k-blocks total / of the dense part; MMA N
-  int t, nb;       // tile, 256-wide N block
+  int t, half, nb; // plan tile, 128-row half (1-SM kernel), 256-wide N block
   int c0, nc;      // chunk range (main: tile's chunks; shrink: item's chunks; reduce: nc)
   ReduceItem ri;
   bool skip;
 };
 
+// Main work item `item` over [tile0, tile0 + n_tiles_rng) x n_nblk, grouped
+// by kGroupM tiles so that concurrently running items share W tiles in L2.
+// `units` = 1 (2-SM kernel: a unit is a 256-row tile) or 2 (1-SM kernel: a
+// unit is a 128-row half).
+__device__ __forceinline__ void raster(const TcParams& p, int item, int units, Item& it) {
+  const int n_units = p.n_tiles_rng * units;
+  const int gm = kGroupM * units;
+  const int per_group = gm * p.n_nblk;
+  const int g = item / per_group, r = item % per_group;
+  const int u0 = g * gm;
+  const int gs = min(gm, n_units - u0);
+  it.nb = r / gs;
+  const int u = u0 + r % gs;
+  it.t = p.tile0 + u / units;
+  it.half = u % units;
+}
+
 template <int MODE>
-__device__ __forceinline__ Item decode(const TcParams& p, int item) {
+__device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
   Item it;
   it.skip = false;
   it.nb = 0;
+  it.half = 0;
   if (MODE == FWD_MAIN || MODE == DX_MAIN) {
-    const int per_group = kGroupM * p.n_nblk;
-    const int g = item / per_group, r = item % per_group;
-    const int t0 = g * kGroupM;
-    const int gs = min(kGroupM, p.n_tiles_rng - t0);
-    it.nb = r / gs;
-    it.t = p.tile0 + t0 + r % gs;
+    raster(p, item, units, it);
     it.c0 = p.plan.tile_chunk_begin[it.t];
     it.nc = p.no_expand ? 0 : p.plan.tile_chunk_begin[it.t + 1] - it.c0;
     it.nk1 = p.nk_main;
     it.nk = it.nk1 + it.nc;
     it.n = kAccCols;
   } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
-    const ShrinkItem s = p.plan.shrink[p.item0 + item];
+    const ShrinkItem s = p.plan.shrink[p.item0 + item / 2];
     it.t = s.tile;
+    it.half = item % 2;
     it.c0 = s.c0;
     it.nc = s.nc;
     it.nk1 = it.nk = p.nk_main;
@@ -207,7 +292,7 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item) {
   } else {
     it.ri = p.plan.reduce[item];
     it.nc = it.ri.nc;
-    it.nk1 = it.nk = 2 * (it.ri.le - it.ri.lb);
+    it.nk1 = it.nk = 4 * (it.ri.le - it.ri.lb);  // 64-row K slices of 256-row blocks
     it.n = 64 * it.nc;
     it.t = 0;
     it.c0 = 0;
@@ -216,14 +301,37 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item) {
   return it;
 }
 
-// ------------------------------------------------------------------ kernel
+// ------------------------------------------------------------------ epilogues
+// Store one 32-column slice of the main accumulator (row `row` of Y / dX).
+template <int MODE>
+__device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row, int n0, int col, bool empty_acc,
+                                               const uint32_t (&v)[32]) {
+  const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
+  if (row >= p.M) return;
+  float f[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) f[q] = empty_acc ? 0.f : __uint_as_float(v[q]);
+  if (MODE == FWD_MAIN && p.bias) {
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
+  }
+  __nv_bfloat16* dst = p.out + row * N + n0 + col;
+  if (n0 + col + 32 <= N) {
+    store32_bf16(dst, f);
+  } else {
+    for (int q = 0; q < 32 && n0 + col + q < N; ++q) dst[q] = __float2bfloat16_rn(f[q]);
+  }
+}
+
+// ------------------------------------------------------------------ 1-SM kernel
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;   // [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages1 * kStage1Bytes);
+  uint64_t* empty = full + kStages1;
+  uint64_t* tfull = empty + kStages1;  // [2]
   uint64_t* tempty = tfull + 2;        // [2]
   uint64_t* drain = tempty + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -232,9 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   constexpr bool A_MN = MODE == REDUCE;
   constexpr bool B_MN = MODE == DX_MAIN || MODE == SHRINK_BWD || MODE == REDUCE;
+  constexpr int kUnits = 2;  // main modes run on 128-row halves of the plan tiles
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStages1; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -261,67 +370,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     // ---------------------------------------------------------------- TMA producer
     int stage = 0;
     uint32_t phase = 0;
-    int issued_parity[kStages];
-    for (int s = 0; s < kStages; ++s) issued_parity[s] = -1;
+    int issued_parity[kStages1];
+    for (int s = 0; s < kStages1; ++s) issued_parity[s] = -1;
     bool ok = true;
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-      const Item it = decode<MODE>(p, item);
+      const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
+      const int row0 = it.t * kTileRows + it.half * kHalfRows;  // first X / dY row of the A tile
       for (int kb = 0; kb < it.nk; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-        uint8_t* sA = smem + stage * kStageBytes;
-        uint8_t* sB = sA + kABytes;
+        uint8_t* sA = smem + stage * kStage1Bytes;
+        uint8_t* sB = sA + kA1Bytes;
         uint64_t* bar = &full[stage];
         if (MODE == FWD_MAIN) {
-          mbar_expect_tx(bar, kABytes + kBBytes);
+          mbar_expect_tx(bar, kStage1Bytes);
           if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0);
             tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256);
           } else {
             const int c = it.c0 + kb - it.nk1;
-            tma_load(sA, &p.mA1, bar, 0, c * 128);
+            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows);
             tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256);
           }
         } else if (MODE == DX_MAIN) {
-          mbar_expect_tx(bar, kABytes + kBBytes);
+          mbar_expect_tx(bar, kStage1Bytes);
           if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0);
             for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64);
           } else {
             const int c = it.c0 + kb - it.nk1;
             const int pcol = p.plan.chunks[c].pcol;
-            tma_load(sA, &p.mA1, bar, 0, c * 128);
+            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows);
             for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol);
           }
         } else if (MODE == SHRINK_FWD) {
-          mbar_expect_tx(bar, kABytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+          mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
+          tma_load(sA, &p.mA0, bar, kb * 64, row0);
           for (int i = 0; i < it.nc; ++i)
             tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol);
         } else if (MODE == SHRINK_BWD) {
-          mbar_expect_tx(bar, kABytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, it.t * 128);
+          mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
+          tma_load(sA, &p.mA0, bar, kb * 64, row0);
           for (int i = 0; i < it.nc; ++i)
             tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64);
-        } else {  // REDUCE
-          const int cb = p.plan.list[it.ri.lb + kb / 2];
-          const int h = kb % 2;
+        } else {  // REDUCE: k-block kb = 64-row slice q of list entry kb / 4
+          const int cb = p.plan.list[it.ri.lb + kb / 4];
+          const int q = kb % 4;
           const int t = p.plan.chunks[cb].tile;
           const CUtensorMap* ma = it.ri.kind == 0 ? &p.mA0 : &p.mA1;
           const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
           mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
-          for (int i = 0; i < 2; ++i) tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * 128 + 64 * h);
+          for (int i = 0; i < 2; ++i)
+            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * kTileRows + 64 * q);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * 128 + 64 * h);
+            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * kTileRows + 64 * q);
         }
         issued_parity[stage] = int(phase);
-        if (++stage == kStages) { stage = 0; phase ^= 1; }
+        if (++stage == kStages1) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok) {
       // let copies already in flight land before the CTA exits
       const unsigned long long t0 = now_ns();
-      for (int s = 0; s < kStages; ++s) {
+      for (int s = 0; s < kStages1; ++s) {
         if (issued_parity[s] < 0) continue;
         while (!mbar_try(su32(&full[s]), uint32_t(issued_parity[s]))) {
           if (now_ns() - t0 > kTimeoutNs) break;
@@ -339,23 +450,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     const uint32_t a_step = A_MN ? (16 * 128) >> 4 : 32 >> 4;  // descriptor units per UMMA_K = 16
     const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-      const Item it = decode<MODE>(p, item);
+      const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(acc * kAccCols);
-      const uint32_t idesc = idesc_bf16(it.n, A_MN, B_MN);
+      const uint32_t idesc = idesc_bf16(128, it.n, A_MN, B_MN);
       for (int kb = 0; kb < it.nk; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sA = su32(smem + stage * kStageBytes);
+        const uint32_t sA = su32(smem + stage * kStage1Bytes);
         const uint64_t ad = sdesc(sA, a_lbo, 1024);
-        const uint64_t bd = sdesc(sA + kABytes, b_lbo, 1024);
+        const uint64_t bd = sdesc(sA + kA1Bytes, b_lbo, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc_mma(d, ad + uint64_t(k * a_step), bd + uint64_t(k * b_step), idesc, (kb | k) != 0);
         tc_commit(&empty[stage]);
-        if (++stage == kStages) { stage = 0; phase ^= 1; }
+        if (++stage == kStages1) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
       tc_commit(&tfull[acc]);
@@ -375,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
-      const Item it = decode<MODE>(p, item);
+      const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
@@ -383,47 +494,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       uint32_t v[32];
       if (MODE == FWD_MAIN || MODE == DX_MAIN) {
         const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-        const int64_t row = int64_t(it.t) * 128 + r;
+        const int64_t row = int64_t(it.t) * kTileRows + it.half * kHalfRows + r;
         const int n0 = it.nb * 256;
         const bool empty_acc = it.nk == 0;  // delta-only call on a tile without LoRA rows
         for (int col = 0; col < kAccCols; col += 32) {
           if (n0 + col >= N) break;
           if (!empty_acc) tc_ld32(tbase + col, v);
-          if (row >= p.M) continue;
-          float f[32];
-#pragma unroll
-          for (int q = 0; q < 32; ++q) f[q] = empty_acc ? 0.f : __uint_as_float(v[q]);
-          if (MODE == FWD_MAIN && p.bias) {
-#pragma unroll
-            for (int q = 0; q < 32; ++q)
-              if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
-          }
-          __nv_bfloat16* dst = p.out + row * N + n0 + col;
-          if (n0 + col + 32 <= N) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
-                                 pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
-          } else {
-            for (int q = 0; q < 32 && n0 + col + q < N; ++q) dst[q] = __float2bfloat16_rn(f[q]);
-          }
+          epi_main_slice<MODE>(p, row, n0, col, empty_acc, v);
         }
       } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
+        const int rt = it.half * kHalfRows + r;  // row inside the 256-row tile
         for (int i = 0; i < it.nc; ++i) {
           const Chunk ch = p.plan.chunks[it.c0 + i];
-          const bool in = r >= ch.lo && r < ch.hi;
-          __nv_bfloat16* dst = p.out + (int64_t(it.c0 + i) * 128 + r) * 64;
+          const bool in = rt >= ch.lo && rt < ch.hi;
+          __nv_bfloat16* dst = p.out + (int64_t(it.c0 + i) * kTileRows + rt) * 64;
           for (int col = 0; col < 64; col += 32) {
             tc_ld32(tbase + i * 64 + col, v);
             float f[32];
 #pragma unroll
             for (int q = 0; q < 32; ++q) f[q] = in ? ch.scale * __uint_as_float(v[q]) : 0.f;
-            uint4* d4 = reinterpret_cast<uint4*>(dst + col);
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
-                                 pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+            store32_bf16(dst + col, f);
           }
         }
       } else {  // REDUCE
@@ -440,13 +530,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
               if (d >= p.d_out) continue;
               __nv_bfloat16* dst = p.dB + int64_t(d) * p.R + pcol + col;
               if (col + 32 <= rvalid) {
-                uint4* d4 = reinterpret_cast<uint4*>(dst);
+                float f[32];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                  d4[q] = make_uint4(pack_bf16(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])),
-                                     pack_bf16(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
-                                     pack_bf16(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
-                                     pack_bf16(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+                for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
+                store32_bf16(dst, f);
               } else {
                 for (int q = 0; q < 32 && col + q < rvalid; ++q) dst[q] = __float2bfloat16_rn(__uint_as_float(v[q]));
               }
@@ -470,6 +557,175 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ------------------------------------------------------------------ 2-SM kernel
+// A cluster of two CTAs (ranks 0 and 1) per 256x256 output tile of FWD_MAIN /
+// DX_MAIN.  CTA r stages rows [128 r, 128 r + 128) of the 256-row A tile and
+// rows (columns for MN-major B) [128 r, 128 r + 128) of the 256-wide B tile.
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2Bytes);
+  uint64_t* empty = full + kStages2;
+  uint64_t* tfull = empty + kStages2;  // [2]
+  uint64_t* tempty = tfull + 2;        // [2]  (used in the even CTA)
+  uint64_t* drain = tempty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t crank = cluster_rank();
+  const bool leader = crank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  constexpr bool B_MN = MODE == DX_MAIN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 256);  // both CTAs' epilogue threads
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued_parity[kStages2];
+    for (int s = 0; s < kStages2; ++s) issued_parity[s] = -1;
+    bool ok = true;
+    for (int item = pair; item < p.n_items && ok; item += n_pairs) {
+      const Item it = decode<MODE>(p, item, 1);
+      const int row0 = it.t * kTileRows + int(crank) * kHalfRows;  // this CTA's A rows
+      const int nh = it.nb * 256 + int(crank) * 128;               // this CTA's half of the N block
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+        uint8_t* sA = smem + stage * kStage2Bytes;
+        uint8_t* sB = sA + kA2Bytes;
+        const uint32_t bar = mapa(su32(&full[stage]), 0);  // the even CTA's barrier
+        if (leader) mbar_expect_tx(&full[stage], 2 * kStage2Bytes);
+        if (kb < it.nk1) {
+          tma_load_pair(sA, &p.mA0, bar, kb * 64, row0);
+          if (MODE == FWD_MAIN) {
+            tma_load_pair(sB, &p.mB0, bar, kb * 64, nh);
+          } else {
+            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB0, bar, nh + 64 * i, kb * 64);
+          }
+        } else {
+          const int c = it.c0 + kb - it.nk1;
+          const int pcol = p.plan.chunks[c].pcol;
+          tma_load_pair(sA, &p.mA1, bar, 0, c * kTileRows + int(crank) * kHalfRows);
+          if (MODE == FWD_MAIN) {
+            tma_load_pair(sB, &p.mB1, bar, pcol, nh);
+          } else {
+            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB1, bar, nh + 64 * i, pcol);
+          }
+        }
+        issued_parity[stage] = int(phase);
+        if (++stage == kStages2) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok && leader) {
+      const unsigned long long t0 = now_ns();
+      for (int s = 0; s < kStages2; ++s) {
+        if (issued_parity[s] < 0) continue;
+        while (!mbar_try(su32(&full[s]), uint32_t(issued_parity[s]))) {
+          if (now_ns() - t0 > kTimeoutNs) break;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    const uint32_t b_lbo = B_MN ? uint32_t(kBox64) : 16u;
+    const uint32_t a_step = 32 >> 4;
+    const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
+    const uint32_t idesc = idesc_bf16(256, 256, false, B_MN);
+    for (int item = pair; item < p.n_items && ok; item += n_pairs) {
+      const Item it = decode<MODE>(p, item, 1);
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d = tmem + uint32_t(acc * kAccCols);
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sA = su32(smem + stage * kStage2Bytes);
+        const uint64_t ad = sdesc(sA, 16u, 1024);
+        const uint64_t bd = sdesc(sA + kA2Bytes, b_lbo, 1024);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_pair(d, ad + uint64_t(k * a_step), bd + uint64_t(k * b_step), idesc, (kb | k) != 0);
+        tc_commit_pair_both(&empty[stage]);
+        if (++stage == kStages2) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      tc_commit_pair_both(&tfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    tc_commit_pair_local(drain);
+    const unsigned long long t0 = now_ns();
+    while (!mbar_try(su32(drain), 0)) {
+      if (now_ns() - t0 > kTimeoutNs) { atomicOr(&g_err_word, kErrTimeout); break; }
+    }
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quad = warp % 4;
+    const int r = quad * 32 + lane;
+    const uint32_t tempty_even[2] = {mapa(su32(&tempty[0]), 0), mapa(su32(&tempty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int item = pair; item < p.n_items; item += n_pairs) {
+      const Item it = decode<MODE>(p, item, 1);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);
+      const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
+      const int64_t row = int64_t(it.t) * kTileRows + int(crank) * kHalfRows + r;
+      const int n0 = it.nb * 256;
+      const bool empty_acc = it.nk == 0;
+      uint32_t v[32];
+      for (int col = 0; col < kAccCols; col += 32) {
+        if (n0 + col >= N) break;
+        if (!empty_acc) tc_ld32(tbase + col, v);
+        epi_main_slice<MODE>(p, row, n0, col, empty_acc, v);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(tempty_even[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  // neither CTA leaves while the other may still touch its shared memory or TMEM
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
@@ -511,16 +767,37 @@ int num_sms() {
   return n;
 }
 
+int cta_budget(int max_ctas) {
+  int sms = num_sms();
+  if (max_ctas > 0 && max_ctas < sms) sms = max_ctas;
+  return sms;
+}
+
 template <int MODE>
-int launch(TcParams& prm, cudaStream_t st) {
+int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
   if (prm.n_items <= 0) return MLORA_OK;
-  const int sms = num_sms();
+  const int sms = cta_budget(max_ctas);
   if (sms <= 0) return MLORA_ERR_CUDA;
-  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1));
   const int grid = prm.n_items < sms ? prm.n_items : sms;
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);
-  k_tc<MODE><<<grid, kThreads, kSmemBytes, st>>>(prm);
+  k_tc<MODE><<<grid, kThreads, kSmem1, st>>>(prm);
+  count_launch();
+  if (timed) timing_end(MODE, st, ev);
+  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+template <int MODE>
+int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
+  if (prm.n_items <= 0) return MLORA_OK;
+  const int sms = cta_budget(max_ctas);
+  if (sms < 2) return MLORA_ERR_UNSUPPORTED;
+  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc2<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
+  const int pairs = std::min(prm.n_items, sms / 2);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  const bool timed = timing_begin(st, ev);
+  k_tc2<MODE><<<2 * pairs, kThreads, kSmem2, st>>>(prm);
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -548,7 +825,7 @@ bool tc_available() {
 
 int tc_forward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
-  const int64_t zrows = int64_t(n_chunks) * 128;
+  const int64_t zrows = int64_t(n_chunks) * kTileRows;
   if (a.t1 <= a.t0) return MLORA_OK;
   if (n_chunks > 0 && (a.stages & MLORA_STAGE_SHRINK)) {
     // shrink items are in tile order: the launch covers those of [t0, t1)
@@ -559,43 +836,48 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || !make_map(&prm.mB0, a.A_pack, a.R, a.d_in, 64))
       return MLORA_ERR_UNSUPPORTED;
     prm.item0 = int(lo - sh.begin());
-    prm.n_items = int(hi - lo);
+    prm.n_items = 2 * int(hi - lo);  // two 128-row halves per shrink item
     prm.nk_main = (a.d_in + 63) / 64;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
-    int s = launch<SHRINK_FWD>(prm, st);
+    int s = launch1<SHRINK_FWD>(prm, st, a.max_ctas);
     if (s != MLORA_OK) return s;
   }
   if (!(a.stages & MLORA_STAGE_MAIN)) return MLORA_OK;
   const bool expand = n_chunks > 0 && !(a.stages & MLORA_STAGE_NO_EXPAND);
+  const int brows = a.pair_mma ? 128 : 256;  // rows of one B box (a CTA's share of the N block)
   TcParams prm = base_params(a);
-  if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, 256)))
+  if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, brows)))
     return MLORA_ERR_UNSUPPORTED;
   if (expand &&
-      (!make_map(&prm.mA1, a.zsave, zrows, 64, 128) || !make_map(&prm.mB1, a.B_pack, a.d_out, a.R, 256)))
+      (!make_map(&prm.mA1, a.zsave, zrows, 64, 128) || !make_map(&prm.mB1, a.B_pack, a.d_out, a.R, brows)))
     return MLORA_ERR_UNSUPPORTED;
   prm.no_expand = expand ? 0 : 1;
   prm.tile0 = a.t0;
   prm.n_tiles_rng = a.t1 - a.t0;
   prm.n_nblk = (a.d_out + 255) / 256;
-  prm.n_items = prm.n_tiles_rng * prm.n_nblk;
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
-  return launch<FWD_MAIN>(prm, st);
+  if (a.pair_mma) {
+    prm.n_items = prm.n_tiles_rng * prm.n_nblk;
+    return launch2<FWD_MAIN>(prm, st, a.max_ctas);
+  }
+  prm.n_items = 2 * prm.n_tiles_rng * prm.n_nblk;
+  return launch1<FWD_MAIN>(prm, st, a.max_ctas);
 }
 
 int tc_backward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
-  const int64_t zrows = int64_t(n_chunks) * 128;
+  const int64_t zrows = int64_t(n_chunks) * kTileRows;
   int s;
   if (n_chunks > 0 && (a.dX || a.dA)) {
     TcParams prm = base_params(a);
     if (!make_map(&prm.mA0, a.dY, a.M, a.d_out, 128) || !make_map(&prm.mB0, a.B_pack, a.d_out, a.R, 64))
       return MLORA_ERR_UNSUPPORTED;
-    prm.n_items = a.plan.n_shrink;
+    prm.n_items = 2 * a.plan.n_shrink;
     prm.nk_main = (a.d_out + 63) / 64;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
-    if ((s = launch<SHRINK_BWD>(prm, st)) != MLORA_OK) return s;
+    if ((s = launch1<SHRINK_BWD>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
   if (a.dX) {
     TcParams prm = base_params(a);
@@ -607,10 +889,16 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.tile0 = 0;
     prm.n_tiles_rng = a.plan.n_tiles;
     prm.n_nblk = (a.d_in + 255) / 256;
-    prm.n_items = a.plan.n_tiles * prm.n_nblk;
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
-    if ((s = launch<DX_MAIN>(prm, st)) != MLORA_OK) return s;
+    if (a.pair_mma) {
+      prm.n_items = a.plan.n_tiles * prm.n_nblk;
+      s = launch2<DX_MAIN>(prm, st, a.max_ctas);
+    } else {
+      prm.n_items = 2 * a.plan.n_tiles * prm.n_nblk;
+      s = launch1<DX_MAIN>(prm, st, a.max_ctas);
+    }
+    if (s != MLORA_OK) return s;
   }
   if (n_chunks > 0 && (a.dA || a.dB)) {
     TcParams prm = base_params(a);
@@ -620,7 +908,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.n_items = a.plan.n_reduce;
     prm.dA = reinterpret_cast<__nv_bfloat16*>(a.dA);
     prm.dB = reinterpret_cast<__nv_bfloat16*>(a.dB);
-    if ((s = launch<REDUCE>(prm, st)) != MLORA_OK) return s;
+    if ((s = launch1<REDUCE>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
   return MLORA_OK;
 }

@@ -29,7 +29,7 @@ F32 = 0
 BF16 = 1
 
 RANK_CHUNK = 64
-TILE_ROWS = 128
+TILE_ROWS = 256
 
 STAGE_SHRINK = 1
 STAGE_MAIN = 2
@@ -38,6 +38,7 @@ STAGE_NO_EXPAND = 4
 IMPL_AUTO = 0
 IMPL_SIMT = 1
 IMPL_TC = 2
+IMPL_TC_1SM = 3
 
 _c_int32_p = ctypes.POINTER(ctypes.c_int32)
 _c_float_p = ctypes.POINTER(ctypes.c_float)
@@ -50,6 +51,7 @@ class Problem(ctypes.Structure):
         ("d_out", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("impl", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32),
     ]
 
 

@@ -21,7 +21,7 @@ from . import _lib
 from ._lib import BF16, F32, RANK_CHUNK, TILE_ROWS
 
 _DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
-_IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC}
+_IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC, "tc1": _lib.IMPL_TC_1SM}
 
 
 def mlora_dtype(dt: torch.dtype) -> int:
@@ -203,8 +203,8 @@ class _CallArgs:
     """Keeps the numpy arrays behind the ctypes structs alive for one call."""
 
     def __init__(self, rows, d_in, d_out, dtype, impl, plan: RoutePlan, table: AdapterTable,
-                 scaling: np.ndarray):
-        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl])
+                 scaling: np.ndarray, max_ctas: int = 0):
+        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas))
         self.seg_start = np.ascontiguousarray(plan.seg_start, dtype=np.int32)
         self.seg_adapter = np.ascontiguousarray(plan.seg_adapter, dtype=np.int32)
         self.rank = np.ascontiguousarray(table.rank, dtype=np.int32)
@@ -233,6 +233,7 @@ class LayerState:
     A_pack: torch.Tensor
     B_pack: torch.Tensor
     impl: str = "auto"
+    max_ctas: int = 0  # cap on persistent-kernel CTAs (0 = one per SM)
 
 
 def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
@@ -265,7 +266,8 @@ class StagedForward:
         self.x, self.W, self.bias, self.st = x, W, bias, st
         rows, d_in = x.shape
         d_out = st.B_pack.shape[0]
-        self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling)
+        self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling,
+                              st.max_ctas)
         zb, wb = self.args.sizes()
         dev = x.device
         self.y = y if y is not None else torch.empty(rows, d_out, dtype=x.dtype, device=dev)
@@ -282,9 +284,17 @@ class StagedForward:
     def shrink(self, t0=0, t1=None):
         self._run(_lib.STAGE_SHRINK, t0, self.n_tiles if t1 is None else t1, None)
 
-    def main(self, t0=0, t1=None, expand=True, add_bias=True):
+    def main(self, t0=0, t1=None, expand=True, add_bias=True, max_ctas=None):
+        """``max_ctas`` (default: the state's) caps the mainloop's CTAs for
+        this call, leaving SMs to concurrent communication kernels."""
         stages = _lib.STAGE_MAIN | (0 if expand else _lib.STAGE_NO_EXPAND)
-        self._run(stages, t0, self.n_tiles if t1 is None else t1, self.bias if add_bias else None)
+        old = self.args.prob.max_ctas
+        if max_ctas is not None:
+            self.args.prob.max_ctas = int(max_ctas)
+        try:
+            self._run(stages, t0, self.n_tiles if t1 is None else t1, self.bias if add_bias else None)
+        finally:
+            self.args.prob.max_ctas = old
 
 
 def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, want_dB: bool):

@@ -51,10 +51,21 @@ def shard_columns(d_in: int, rank: int, world: int, align: int = 64) -> Tuple[in
 
 
 class NativeCompute:
-    """The native kernels (tcgen05 for bf16) behind the sharded layer."""
+    """The native kernels (tcgen05 for bf16) behind the sharded layer.
+    ``comm_sms`` SMs are left out of the nano-batch mainloops so the NCCL
+    all-reduce of the previous nano-batch has SMs to run on."""
 
-    def __init__(self, impl: str = "auto"):
+    def __init__(self, impl: str = "auto", comm_sms: int = 16):
         self.impl = impl
+        self.comm_sms = int(comm_sms)
+        self._sms = None
+
+    def _main_ctas(self, device):
+        if self.comm_sms <= 0:
+            return 0
+        if self._sms is None:
+            self._sms = torch.cuda.get_device_properties(device).multi_processor_count
+        return max(1, self._sms - self.comm_sms)
 
     def begin(self, layer, x_p, plan):
         st = ops.LayerState(layer.table, layer.scaling, plan, layer.A_pack, layer.B_pack, self.impl)
@@ -68,7 +79,7 @@ class NativeCompute:
         ctx["fw"].shrink()
 
     def main(self, ctx, t0, t1, expand, add_bias):
-        ctx["fw"].main(t0, t1, expand=expand, add_bias=add_bias)
+        ctx["fw"].main(t0, t1, expand=expand, add_bias=add_bias, max_ctas=self._main_ctas(ctx["fw"].x.device))
 
     def backward(self, ctx, layer, x_p, dy):
         return ops.backward_raw(dy, x_p, layer.W, ctx["fw"].z, ctx["st"], True, True, True)
@@ -190,11 +201,18 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    # SMs the nano-batch mainloops leave to NCCL, and NCCL's channel (CTA)
+    # count matched to them so every channel of an all-reduce is resident
+    # while the next nano-batch computes; both fixed before the communicator
+    # exists, overridable from the environment
+    comm_sms = int(os.environ.get("MLORA_COMM_SMS", "16"))
+    os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, comm_sms)))
+    os.environ.setdefault("NCCL_MIN_NCHANNELS", str(max(1, comm_sms)))
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
         sp = workloads.spec(args.workload)
         w = workloads.build(sp, device=dev)
-        layer = ShardedLayer(w.model, rank, world)
+        layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms))
         x_p = layer.shard_input(w.x)
         plan = ops.route(w.ids, layer.table, dev)
         lr = sp.lr
@@ -217,6 +235,15 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
             nxt, why = ctl.observe(t)
             horizons.append({"n": n, "ms": round(t, 4), "decision": why, "next_n": nxt})
         best_n = ctl.best_n
+
+        # SMs left to NCCL during the nano-batch mainloops (the persistent
+        # mainloop would otherwise hold every SM and serialise the all-reduce)
+        sm_sweep = {}
+        for k in sorted({0, comm_sms // 2, comm_sms, comm_sms + comm_sms // 2}):
+            layer.compute.comm_sms = k
+            sm_sweep[k] = _timed(stepper(best_n), 3, dev)
+        best_k = min(sm_sweep, key=sm_sweep.get)
+        layer.compute.comm_sms = best_k
 
         # overlap accounting at the chosen N
         t_pipe = _timed(stepper(best_n), 3, dev)
@@ -259,7 +286,9 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
                        "parallelism": f"K-shard x{world} + nano-batch pipeline (AIMD N={best_n})",
                        "l2": "per-step traffic (Y all-reduce, 1.4 GiB) larger than L2"},
             "step_tflops": round(step_flops / (ms / 1000.0) / 1e12, 1),
-            "overlap": {"n": best_n, "pipelined_ms": round(t_pipe, 4), "serial_ms": round(t_serial, 4),
+            "overlap": {"n": best_n, "comm_sms": best_k, "nccl_channels": os.environ.get("NCCL_MAX_NCHANNELS"),
+                        "comm_sms_sweep_ms": {str(k): round(v, 4) for k, v in sm_sweep.items()},
+                        "pipelined_ms": round(t_pipe, 4), "serial_ms": round(t_serial, 4),
                         "compute_only_ms": round(t_compute, 4), "comm_only_ms": round(t_comm, 4),
                         "comm_hidden_frac": round(hidden, 4)},
             "aimd": horizons,

@@ -141,7 +141,7 @@ def test_config0_fp32_full_size():
 
 
 @pytest.mark.parametrize("cfg,scale", [("c1", 0.125), ("c2", 0.0625), ("c3", 0.0625), ("c4", 0.03125)])
-@pytest.mark.parametrize("impl", ["tc", "simt"])
+@pytest.mark.parametrize("impl", ["tc", "tc1", "simt"])
 def test_bf16_configs_scaled(cfg, scale, impl):
     """bf16 configurations at reduced size: native kernels vs the fp64 oracle
     on the same bf16-rounded inputs."""
@@ -178,11 +178,12 @@ EDGE_CASES = {
 }
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc"), (torch.bfloat16, "tc1")])
 @pytest.mark.parametrize("case", sorted(EDGE_CASES))
-def test_edge_cases(case, dtype):
+def test_edge_cases(case, dtype, impl):
     d_in, d_out, ranks, idf = EDGE_CASES[case]
     m = _edge_module(d_in, d_out, ranks, dtype)
+    m.impl = impl
     ids = torch.tensor(idf(), dtype=torch.int64, device=DEV)
     g = torch.Generator(device=DEV).manual_seed(11)
     x = torch.randn(ids.shape[0], d_in, generator=g, device=DEV).to(dtype)
@@ -191,10 +192,11 @@ def test_edge_cases(case, dtype):
     assert_parity(module_step(m, x, ids, dy), oracle_step(m, x, ids, dy), tol, case)
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_delta_only(dtype):
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc"), (torch.bfloat16, "tc1")])
+def test_delta_only(dtype, impl):
     """add_base=False: only the LoRA delta (the reference kernel's ADD_BASE=False)."""
     m = _edge_module(256, 256, {0: 8, 1: 16, 2: 64}, dtype, bias_std=0.0)
+    m.impl = impl
     ids = torch.tensor([0] * 100 + [1] * 200 + [2] * 37, device=DEV)
     x = torch.randn(ids.shape[0], 256, device=DEV).to(dtype)
     dy = torch.randn(ids.shape[0], 256, device=DEV).to(dtype)
@@ -205,14 +207,17 @@ def test_delta_only(dtype):
 
 
 def test_tc_matches_simt_bf16():
-    """The two kernel families agree on the same bf16 inputs."""
+    """The kernel families agree on the same bf16 inputs; the 2-SM and 1-SM
+    mainloops accumulate identically (same K order), so they agree bit for bit."""
     w = workloads.build(workloads.spec("c1", 0.125), device=DEV)
-    w.model.impl = "tc"
-    a = module_step(w.model, w.x, w.ids, w.dy)
-    w.model.impl = "simt"
-    b = module_step(w.model, w.x, w.ids, w.dy)
-    for u, v in zip(a[:2], b[:2]):
+    outs = {}
+    for impl in ("tc", "tc1", "simt"):
+        w.model.impl = impl
+        outs[impl] = module_step(w.model, w.x, w.ids, w.dy)
+    for u, v in zip(outs["tc"][:2], outs["simt"][:2]):
         assert orc.relative_l2(u, v) <= 1e-2
+    for u, v in zip(outs["tc"][:2], outs["tc1"][:2]):
+        assert np.array_equal(u, v)
 
 
 def test_independent_adapter_forward():

@@ -43,8 +43,8 @@ def test_status_strings_and_sizes_without_gpu():
     plan = ops.RoutePlan(300, np.array([0, 100, 101, 300], np.int32), np.array([0, 1, 2], np.int32))
     args = ops._CallArgs(300, 256, 128, _lib.BF16, "auto", plan, table, np.ones(3, np.float32))
     zb, wb = args.sizes()
-    # tiles: [0,128) has seg0 (1 chunk), seg1 (2 chunks), seg2 (1 chunk) -> 4; [128,256) seg2 -> 1; [256,300) seg2 -> 1
-    assert zb == 6 * 128 * 64 * 2
+    # 256-row tiles: [0,256) has seg0 (1 chunk), seg1 (2 chunks), seg2 (1 chunk) -> 4; [256,300) seg2 -> 1
+    assert zb == 5 * 256 * 64 * 2
     assert wb >= zb
     # invalid routing is rejected with ValueError
     bad = ops.RoutePlan(300, np.array([0, 100, 99, 300], np.int32), np.array([0, 1, 2], np.int32))

@@ -19,7 +19,7 @@ from tlora_b200.overlap import ShardedLayer, shard_columns
 from tlora_b200.nano import split_ranges
 from tlora_b200 import ops
 
-TILE = 128
+from tlora_b200._lib import TILE_ROWS as TILE  # noqa: E402
 
 
 class DenseCompute:
