@@ -40,9 +40,12 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4"])
+    p.add_argument("--rows-scale", type=float, default=1.0,
+                   help="scale the rows of every adapter (profiling captures of a smaller case)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernels", default="auto", choices=["auto", "tc", "tc1", "simt"],
-                   help="kernel family of the module (tc = 2-SM pair mainloops, tc1 = 1-SM)")
+    p.add_argument("--kernels", default="auto", choices=["auto", "tc", "tc1", "tc2", "simt"],
+                   help="kernel family of the module (tc: per-role best mainloops; tc1: all single-SM; "
+                        "tc2: all on 2-SM pairs)")
     p.add_argument("--no-cublas", action="store_true", help="skip the cuBLAS backbone-GEMM context measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU time of the baseline sample")
     return p.parse_args()
@@ -194,13 +197,17 @@ def run_single(args, peaks_d, peaks_kind):
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    sp = workloads.spec(args.workload)
+    sp = workloads.spec(args.workload, rows_scale=args.rows_scale)
     w = workloads.build(sp, device=dev)
     m = w.model
     m.impl = args.kernels
     x = w.x.requires_grad_(True)
     lr = sp.lr
-    step_fn = (lambda: train_step(m, x, w.ids, w.dy, lr)) if sp.train else (lambda: m(x, w.ids))
+    # per-row adapter ids as the job packer produces them: on the host (the
+    # reference's packed batches carry host-side spans, phase5c_fused_triton.py:338-377);
+    # routing them is a vectorised host pass with no device synchronisation
+    ids_host = w.ids.cpu()
+    step_fn = (lambda: train_step(m, x, ids_host, w.dy, lr)) if sp.train else (lambda: m(x, ids_host))
 
     # warm-up
     with torch.no_grad() if not sp.train else torch.enable_grad():
@@ -230,30 +237,52 @@ def run_single(args, peaks_d, peaks_kind):
     ktimes = _lib.timing_read()
     ms = e0.elapsed_time(e1) / args.steps
 
-    # end to end through the module API: pinned host X and ids, H2D inside the
-    # timed region, D2H read of a result probe every step
+    # end to end through the module API: every step copies its X from pinned
+    # host memory (on a copy stream, double-buffered so the copy of step i+1
+    # overlaps the compute of step i, as a data loader's prefetch does) and
+    # reads a probe of the updated adapter weights back to the host
     x_host = w.x.detach().cpu().pin_memory()
     ids_host = w.ids.cpu()
-    x_dev = torch.empty_like(w.x).requires_grad_(True)
+    bufs = [torch.empty_like(w.x.detach()) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    copy_stream = torch.cuda.Stream(dev)
     probe = torch.empty(64, dtype=w.x.dtype).pin_memory()
     a0 = m.adapters["0"].A
+    compute = torch.cuda.current_stream(dev)
 
-    def e2e_step():
-        with torch.no_grad():
-            x_dev.copy_(x_host, non_blocking=True)
-        train_step(m, x_dev, ids_host, w.dy, lr)
+    def issue_copy(i):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(consumed[i % 2])
+            bufs[i % 2].copy_(x_host, non_blocking=True)
+            copied[i % 2].record(copy_stream)
+
+    def e2e_step(i):
+        compute.wait_event(copied[i % 2])
+        issue_copy(i + 1)  # prefetch the next step's X
+        xi = bufs[i % 2].detach().requires_grad_(sp.train)
+        if sp.train:
+            train_step(m, xi, ids_host, w.dy, lr)
+        else:
+            with torch.no_grad():
+                m(xi, ids_host)
+        consumed[i % 2].record(compute)
         probe.copy_(a0.detach()[0, :64], non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        compute.synchronize()
         return float(probe[0])
 
-    for _ in range(2):
-        e2e_step()
+    for ev in consumed:
+        ev.record(compute)
+    issue_copy(0)
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
     n_e2e = max(3, args.steps // 2)
-    for _ in range(n_e2e):
-        e2e_step()
+    t0 = time.perf_counter()
+    for i in range(2, 2 + n_e2e):
+        e2e_step(i)
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / n_e2e
+    torch.cuda.synchronize()
 
     cublas = None if args.no_cublas else cublas_backbone(w, dev)
 

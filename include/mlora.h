@@ -64,8 +64,10 @@ extern "C" {
 /* kernel family selection for mlora_forward / mlora_backward */
 #define MLORA_IMPL_AUTO 0   /* tcgen05 tensor-core kernels when the shape allows, else SIMT */
 #define MLORA_IMPL_SIMT 1   /* CUDA-core kernels, fp32 accumulate (exact fp32 mode) */
-#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only); mainloops on 2-SM pairs */
-#define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with single-SM mainloops (comparison path) */
+#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only); forward mainloop on single
+                               SMs, dX mainloop on 2-SM pairs (the faster variant of each, measured) */
+#define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with both mainloops on single SMs (comparison path) */
+#define MLORA_IMPL_TC_2SM 4 /* as MLORA_IMPL_TC with both mainloops on 2-SM pairs (comparison path) */
 
 typedef struct mlora_problem {
   int64_t rows;   /* M: rows of X in this call */

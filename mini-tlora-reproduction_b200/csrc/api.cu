@@ -54,7 +54,7 @@ bool tc_shape_ok(const mlora_problem* prob) {
 
 int choose_impl(const mlora_problem* prob) {
   if (prob->impl == MLORA_IMPL_SIMT) return MLORA_IMPL_SIMT;
-  if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM)
+  if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM || prob->impl == MLORA_IMPL_TC_2SM)
     return tc_shape_ok(prob) ? MLORA_IMPL_TC : -1;
   if (prob->impl != MLORA_IMPL_AUTO) return -1;
   return (tc_shape_ok(prob) && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
@@ -122,7 +122,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
     a.Y = Y; a.zsave = zsave;
     a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
     a.max_ctas = prob->max_ctas;
-    a.pair_mma = prob->impl != MLORA_IMPL_TC_1SM;
+    a.pair_fwd = prob->impl == MLORA_IMPL_TC_2SM;
     return tc_forward(a, s);
   }
   SimtCall a;
@@ -176,7 +176,7 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
     a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
     a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
     a.max_ctas = prob->max_ctas;
-    a.pair_mma = prob->impl != MLORA_IMPL_TC_1SM;
+    a.pair_dx = prob->impl != MLORA_IMPL_TC_1SM;
     return tc_backward(a, s);
   }
   SimtCall a;

@@ -59,17 +59,20 @@ constexpr int kHalfRows = 128;       // rows of one CTA's A tile = TMEM lanes
 constexpr int kStages1 = 4;
 constexpr int kA1Bytes = 128 * 64 * 2;
 constexpr int kStage1Bytes = kA1Bytes + 256 * 64 * 2;
-constexpr int kSmem1 = kStages1 * kStage1Bytes + 1024 + 256;
+// epilogue staging: per epilogue warp two 32x32 bf16 buffers (64-byte swizzle)
+constexpr int kStageOutBytes = 4 * 2 * 32 * 32 * 2;  // 16 KB
+constexpr int kSmem1 = kStages1 * kStage1Bytes + kStageOutBytes + 1024 + 256;
 // 2-SM kernel: per CTA A 128x64 (16 KB) + B half 128x64 (16 KB) per stage
 constexpr int kStages2 = 6;
 constexpr int kA2Bytes = 128 * 64 * 2;
 constexpr int kStage2Bytes = kA2Bytes + 128 * 64 * 2;
-constexpr int kSmem2 = kStages2 * kStage2Bytes + 1024 + 256;
+constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOutBytes + 1024 + 256;
 
 enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
 
 struct TcParams {
   CUtensorMap mA0, mB0, mA1, mB1;
+  CUtensorMap mY;  // main modes: output [rows, N], 32x32 box, 64-byte swizzle (TMA store)
   PlanDev plan;
   int64_t M;
   int d_in, d_out, R;
@@ -152,21 +155,54 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+// L2 eviction policies for TMA loads: operands reused by many tiles (W,
+// A_pack, B_pack) are kept, operands streamed once (X, dY in the HBM-bound
+// roles) leave first.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                         uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          su32(dst)),
-      "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
+      "l"(map), "r"(su32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 // Load into this CTA's shared memory, completing on the barrier at the
 // shared::cluster address `bar` (the even CTA's barrier of the pair).
-__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y,
+                                              uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          su32(dst)),
-      "l"(map), "r"(bar), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+// TMA store of a 32x32 bf16 box from shared memory, tracked as a bulk group
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -303,24 +339,60 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
 
 // ------------------------------------------------------------------ epilogues
 // Store one 32-column slice of the main accumulator (row `row` of Y / dX).
+// One 32-column slice of the main accumulator for the 32 rows of this warp
+// (rows row_w0 .. row_w0 + 31 of Y / dX, lane = row): TMEM -> registers
+// (+ bias) -> bf16 in the warp's staging buffer -> one TMA store.  Warp-
+// collective: every lane calls it with the same arguments but its own TMEM
+// lane.  `buf` alternates between the warp's two buffers; the store issued
+// from the same buffer two slices earlier must have finished reading it.
 template <int MODE>
-__device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row, int n0, int col, bool empty_acc,
-                                               const uint32_t (&v)[32]) {
+__device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0, int n0, int col, bool empty_acc,
+                                               uint32_t taddr, uint32_t buf, int lane) {
   const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-  if (row >= p.M) return;
   float f[32];
+  if (!empty_acc) {
+    uint32_t v[32];
+    tc_ld32(taddr, v);
 #pragma unroll
-  for (int q = 0; q < 32; ++q) f[q] = empty_acc ? 0.f : __uint_as_float(v[q]);
-  if (MODE == FWD_MAIN && p.bias) {
-#pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
-  }
-  __nv_bfloat16* dst = p.out + row * N + n0 + col;
-  if (n0 + col + 32 <= N) {
-    store32_bf16(dst, f);
+    for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
   } else {
-    for (int q = 0; q < 32 && n0 + col + q < N; ++q) dst[q] = __float2bfloat16_rn(f[q]);
+#pragma unroll
+    for (int q = 0; q < 32; ++q) f[q] = 0.f;
+  }
+  if (MODE == FWD_MAIN && p.bias) {
+    if (n0 + col + 32 <= N) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + col);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(b4 + q);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
+          f[8 * q + 2 * e] += __low2float(h);
+          f[8 * q + 2 * e + 1] += __high2float(h);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q)
+        if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
+    }
+  }
+  if (lane == 0) bulk_wait_read_1();
+  __syncwarp();
+  // row `lane` of the 32x32 box: 64 bytes, 16-byte chunk q at q ^ ((lane >> 1) & 3)
+  const uint32_t rowb = buf + uint32_t(lane) * 64u;
+  const uint32_t sw = uint32_t(lane >> 1) & 3u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    sts128(rowb + ((uint32_t(q) ^ sw) << 4), pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+           pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (row_w0 < p.M) tma_store(&p.mY, buf, n0 + col, int(row_w0));
+    bulk_commit();
   }
 }
 
@@ -329,7 +401,8 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages1 * kStage1Bytes);
+  uint8_t* stage_out = smem + kStages1 * kStage1Bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
   uint64_t* empty = full + kStages1;
   uint64_t* tfull = empty + kStages1;  // [2]
   uint64_t* tempty = tfull + 2;        // [2]
@@ -370,9 +443,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     // ---------------------------------------------------------------- TMA producer
     int stage = 0;
     uint32_t phase = 0;
-    int issued_parity[kStages1];
-    for (int s = 0; s < kStages1; ++s) issued_parity[s] = -1;
+    uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
     bool ok = true;
+    const uint64_t pol_keep = policy_evict_last(), pol_stream = policy_evict_first(),
+                   pol_norm = policy_evict_normal();
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
@@ -385,34 +459,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         if (MODE == FWD_MAIN) {
           mbar_expect_tx(bar, kStage1Bytes);
           if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, row0);
-            tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
+            tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256, pol_keep);
           } else {
             const int c = it.c0 + kb - it.nk1;
-            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows);
-            tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256);
+            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
+            tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256, pol_keep);
           }
         } else if (MODE == DX_MAIN) {
           mbar_expect_tx(bar, kStage1Bytes);
           if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, row0);
-            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
+            for (int i = 0; i < 4; ++i)
+              tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64, pol_keep);
           } else {
             const int c = it.c0 + kb - it.nk1;
             const int pcol = p.plan.chunks[c].pcol;
-            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows);
-            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol);
+            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
+            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol, pol_keep);
           }
         } else if (MODE == SHRINK_FWD) {
           mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, row0);
+          tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol);
+            tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol, pol_keep);
         } else if (MODE == SHRINK_BWD) {
           mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, row0);
+          tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64);
+            tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64, pol_keep);
         } else {  // REDUCE: k-block kb = 64-row slice q of list entry kb / 4
           const int cb = p.plan.list[it.ri.lb + kb / 4];
           const int q = kb % 4;
@@ -421,11 +496,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
           const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
           mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
           for (int i = 0; i < 2; ++i)
-            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * kTileRows + 64 * q);
+            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * kTileRows + 64 * q, pol_stream);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * kTileRows + 64 * q);
+            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * kTileRows + 64 * q, pol_norm);
         }
-        issued_parity[stage] = int(phase);
+        issued |= 1u << stage;
+        issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
         if (++stage == kStages1) { stage = 0; phase ^= 1; }
       }
     }
@@ -433,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       // let copies already in flight land before the CTA exits
       const unsigned long long t0 = now_ns();
       for (int s = 0; s < kStages1; ++s) {
-        if (issued_parity[s] < 0) continue;
-        while (!mbar_try(su32(&full[s]), uint32_t(issued_parity[s]))) {
+        if (!((issued >> s) & 1u)) continue;
+        while (!mbar_try(su32(&full[s]), (issued_par >> s) & 1u)) {
           if (now_ns() - t0 > kTimeoutNs) break;
         }
       }
@@ -483,6 +559,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
     const int r = quad * 32 + lane;  // accumulator row = TMEM lane
+    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 4096u;
+    uint32_t slices = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
@@ -494,13 +572,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       uint32_t v[32];
       if (MODE == FWD_MAIN || MODE == DX_MAIN) {
         const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-        const int64_t row = int64_t(it.t) * kTileRows + it.half * kHalfRows + r;
+        const int64_t row_w0 = int64_t(it.t) * kTileRows + it.half * kHalfRows + quad * 32;
         const int n0 = it.nb * 256;
         const bool empty_acc = it.nk == 0;  // delta-only call on a tile without LoRA rows
         for (int col = 0; col < kAccCols; col += 32) {
           if (n0 + col >= N) break;
-          if (!empty_acc) tc_ld32(tbase + col, v);
-          epi_main_slice<MODE>(p, row, n0, col, empty_acc, v);
+          epi_main_slice<MODE>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
+          ++slices;
         }
       } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
         const int rt = it.half * kHalfRows + r;  // row inside the 256-row tile
@@ -535,12 +613,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
                 for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
                 store32_bf16(dst, f);
               } else {
-                for (int q = 0; q < 32 && col + q < rvalid; ++q) dst[q] = __float2bfloat16_rn(__uint_as_float(v[q]));
+#pragma unroll
+                for (int q = 0; q < 32; ++q)
+                  if (col + q < rvalid) dst[q] = __float2bfloat16_rn(__uint_as_float(v[q]));
               }
             } else {
               if (d >= p.d_in) continue;
-              for (int q = 0; q < 32 && col + q < rvalid; ++q)
-                p.dA[int64_t(pcol + col + q) * p.d_in + d] = __float2bfloat16_rn(__uint_as_float(v[q]));
+#pragma unroll
+              for (int q = 0; q < 32; ++q)
+                if (col + q < rvalid)
+                  p.dA[int64_t(pcol + col + q) * p.d_in + d] = __float2bfloat16_rn(__uint_as_float(v[q]));
             }
           }
         }
@@ -550,6 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -568,7 +651,8 @@ template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2Bytes);
+  uint8_t* stage_out = smem + kStages2 * kStage2Bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
   uint64_t* empty = full + kStages2;
   uint64_t* tfull = empty + kStages2;  // [2]
   uint64_t* tempty = tfull + 2;        // [2]  (used in the even CTA)
@@ -610,9 +694,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     // ---------------------------------------------------------------- TMA producer (both CTAs)
     int stage = 0;
     uint32_t phase = 0;
-    int issued_parity[kStages2];
-    for (int s = 0; s < kStages2; ++s) issued_parity[s] = -1;
+    uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
     bool ok = true;
+    const uint64_t pol_keep = policy_evict_last(), pol_norm = policy_evict_normal();
     for (int item = pair; item < p.n_items && ok; item += n_pairs) {
       const Item it = decode<MODE>(p, item, 1);
       const int row0 = it.t * kTileRows + int(crank) * kHalfRows;  // this CTA's A rows
@@ -624,31 +708,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
         const uint32_t bar = mapa(su32(&full[stage]), 0);  // the even CTA's barrier
         if (leader) mbar_expect_tx(&full[stage], 2 * kStage2Bytes);
         if (kb < it.nk1) {
-          tma_load_pair(sA, &p.mA0, bar, kb * 64, row0);
+          tma_load_pair(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
           if (MODE == FWD_MAIN) {
-            tma_load_pair(sB, &p.mB0, bar, kb * 64, nh);
+            tma_load_pair(sB, &p.mB0, bar, kb * 64, nh, pol_keep);
           } else {
-            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB0, bar, nh + 64 * i, kb * 64);
+            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB0, bar, nh + 64 * i, kb * 64, pol_keep);
           }
         } else {
           const int c = it.c0 + kb - it.nk1;
           const int pcol = p.plan.chunks[c].pcol;
-          tma_load_pair(sA, &p.mA1, bar, 0, c * kTileRows + int(crank) * kHalfRows);
+          tma_load_pair(sA, &p.mA1, bar, 0, c * kTileRows + int(crank) * kHalfRows, pol_norm);
           if (MODE == FWD_MAIN) {
-            tma_load_pair(sB, &p.mB1, bar, pcol, nh);
+            tma_load_pair(sB, &p.mB1, bar, pcol, nh, pol_keep);
           } else {
-            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB1, bar, nh + 64 * i, pcol);
+            for (int i = 0; i < 2; ++i) tma_load_pair(sB + i * kBox64, &p.mB1, bar, nh + 64 * i, pcol, pol_keep);
           }
         }
-        issued_parity[stage] = int(phase);
+        issued |= 1u << stage;
+        issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
         if (++stage == kStages2) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok && leader) {
       const unsigned long long t0 = now_ns();
       for (int s = 0; s < kStages2; ++s) {
-        if (issued_parity[s] < 0) continue;
-        while (!mbar_try(su32(&full[s]), uint32_t(issued_parity[s]))) {
+        if (!((issued >> s) & 1u)) continue;
+        while (!mbar_try(su32(&full[s]), (issued_par >> s) & 1u)) {
           if (now_ns() - t0 > kTimeoutNs) break;
         }
       }
@@ -694,8 +779,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
   } else if (warp >= 2) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quad = warp % 4;
-    const int r = quad * 32 + lane;
-    const uint32_t tempty_even[2] = {mapa(su32(&tempty[0]), 0), mapa(su32(&tempty[1]), 0)};
+    const uint32_t tempty_even0 = mapa(su32(&tempty[0]), 0), tempty_even1 = mapa(su32(&tempty[1]), 0);
+    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 4096u;
+    uint32_t slices = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int item = pair; item < p.n_items; item += n_pairs) {
@@ -704,20 +790,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);
       const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-      const int64_t row = int64_t(it.t) * kTileRows + int(crank) * kHalfRows + r;
+      const int64_t row_w0 = int64_t(it.t) * kTileRows + int(crank) * kHalfRows + quad * 32;
       const int n0 = it.nb * 256;
       const bool empty_acc = it.nk == 0;
-      uint32_t v[32];
       for (int col = 0; col < kAccCols; col += 32) {
         if (n0 + col >= N) break;
-        if (!empty_acc) tc_ld32(tbase + col, v);
-        epi_main_slice<MODE>(p, row, n0, col, empty_acc, v);
+        epi_main_slice<MODE>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
+        ++slices;
       }
       tc_fence_before();
-      mbar_arrive_cluster(tempty_even[acc]);
+      mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
   // neither CTA leaves while the other may still touch its shared memory or TMEM
@@ -746,18 +832,23 @@ EncodeFn get_encode() {
   return fn;
 }
 
-// 2-D bf16 map over a row-major [rows, cols] matrix; box = 64 columns x box_rows
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+// 2-D bf16 map over a row-major [rows, cols] matrix; box = box_cols x box_rows
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int box_cols = 64,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeFn enc = get_encode();
   if (!enc || rows < 1 || cols < 1) return false;
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (cols * 2) % 16 != 0) return false;
   cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
   cuuint64_t strides[1] = {cuuint64_t(cols * 2)};
-  cuuint32_t box[2] = {64u, cuuint32_t(box_rows)};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// store map of a main output [rows, cols]: 32x32 boxes, 64-byte swizzle
+bool make_out_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols) {
+  return make_map(m, base, rows, cols, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 int num_sms() {
@@ -844,7 +935,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   }
   if (!(a.stages & MLORA_STAGE_MAIN)) return MLORA_OK;
   const bool expand = n_chunks > 0 && !(a.stages & MLORA_STAGE_NO_EXPAND);
-  const int brows = a.pair_mma ? 128 : 256;  // rows of one B box (a CTA's share of the N block)
+  const int brows = a.pair_fwd ? 128 : 256;  // rows of one B box (a CTA's share of the N block)
   TcParams prm = base_params(a);
   if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, brows)))
     return MLORA_ERR_UNSUPPORTED;
@@ -858,7 +949,8 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
-  if (a.pair_mma) {
+  if (!make_out_map(&prm.mY, a.Y, a.M, a.d_out)) return MLORA_ERR_UNSUPPORTED;
+  if (a.pair_fwd) {
     prm.n_items = prm.n_tiles_rng * prm.n_nblk;
     return launch2<FWD_MAIN>(prm, st, a.max_ctas);
   }
@@ -891,7 +983,8 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.n_nblk = (a.d_in + 255) / 256;
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
-    if (a.pair_mma) {
+    if (!make_out_map(&prm.mY, a.dX, a.M, a.d_in)) return MLORA_ERR_UNSUPPORTED;
+    if (a.pair_dx) {
       prm.n_items = a.plan.n_tiles * prm.n_nblk;
       s = launch2<DX_MAIN>(prm, st, a.max_ctas);
     } else {

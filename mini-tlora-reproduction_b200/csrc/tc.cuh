@@ -21,7 +21,8 @@ struct TcCall {
   int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
   int t0 = 0, t1 = 0;
   int max_ctas = 0;  // 0 = one CTA per SM
-  bool pair_mma = true;  // mainloops on 2-SM pairs (tcgen05 cta_group::2)
+  bool pair_fwd = false;  // forward mainloop on 2-SM pairs (tcgen05 cta_group::2)
+  bool pair_dx = true;    // dX mainloop on 2-SM pairs
 };
 
 // true when the driver exposes cuTensorMapEncodeTiled and the current device

@@ -21,7 +21,8 @@ from . import _lib
 from ._lib import BF16, F32, RANK_CHUNK, TILE_ROWS
 
 _DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
-_IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC, "tc1": _lib.IMPL_TC_1SM}
+_IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC, "tc1": _lib.IMPL_TC_1SM,
+          "tc2": _lib.IMPL_TC_2SM}
 
 
 def mlora_dtype(dt: torch.dtype) -> int:

@@ -69,15 +69,16 @@ def _zipf_counts(rng: np.random.Generator, n: int, total: int, s: float, n_empty
     return [int(c) for c in counts]
 
 
-def spec(name: str, scale: float = 1.0) -> WorkloadSpec:
+def spec(name: str, scale: float = 1.0, rows_scale: float = 1.0) -> WorkloadSpec:
     """The named configuration.  ``scale`` < 1 shrinks rows and features
-    (rounded to multiples of 64) for parity tests the oracle can finish."""
+    (rounded to multiples of 64) for parity tests the oracle can finish;
+    ``rows_scale`` shrinks the rows only (same layer shape)."""
 
     def d(v):
         return max(64, int(round(v * scale / 64)) * 64)
 
     def rows(v):
-        return max(1, int(round(v * scale)))
+        return max(1, int(round(v * scale * rows_scale)))
 
     if name == "c0":
         return WorkloadSpec("c0", d(1024), d(1024), [4, 8, 16, 32], [rows(c) for c in (64, 128, 192, 256)],

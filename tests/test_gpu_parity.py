@@ -141,7 +141,7 @@ def test_config0_fp32_full_size():
 
 
 @pytest.mark.parametrize("cfg,scale", [("c1", 0.125), ("c2", 0.0625), ("c3", 0.0625), ("c4", 0.03125)])
-@pytest.mark.parametrize("impl", ["tc", "tc1", "simt"])
+@pytest.mark.parametrize("impl", ["tc", "tc1", "tc2", "simt"])
 def test_bf16_configs_scaled(cfg, scale, impl):
     """bf16 configurations at reduced size: native kernels vs the fp64 oracle
     on the same bf16-rounded inputs."""
@@ -178,7 +178,7 @@ EDGE_CASES = {
 }
 
 
-@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc"), (torch.bfloat16, "tc1")])
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2")])
 @pytest.mark.parametrize("case", sorted(EDGE_CASES))
 def test_edge_cases(case, dtype, impl):
     d_in, d_out, ranks, idf = EDGE_CASES[case]
@@ -192,7 +192,7 @@ def test_edge_cases(case, dtype, impl):
     assert_parity(module_step(m, x, ids, dy), oracle_step(m, x, ids, dy), tol, case)
 
 
-@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc"), (torch.bfloat16, "tc1")])
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2")])
 def test_delta_only(dtype, impl):
     """add_base=False: only the LoRA delta (the reference kernel's ADD_BASE=False)."""
     m = _edge_module(256, 256, {0: 8, 1: 16, 2: 64}, dtype, bias_std=0.0)
@@ -211,13 +211,14 @@ def test_tc_matches_simt_bf16():
     mainloops accumulate identically (same K order), so they agree bit for bit."""
     w = workloads.build(workloads.spec("c1", 0.125), device=DEV)
     outs = {}
-    for impl in ("tc", "tc1", "simt"):
+    for impl in ("tc", "tc1", "tc2", "simt"):
         w.model.impl = impl
         outs[impl] = module_step(w.model, w.x, w.ids, w.dy)
     for u, v in zip(outs["tc"][:2], outs["simt"][:2]):
         assert orc.relative_l2(u, v) <= 1e-2
-    for u, v in zip(outs["tc"][:2], outs["tc1"][:2]):
-        assert np.array_equal(u, v)
+    for other in ("tc1", "tc2"):
+        for u, v in zip(outs["tc"][:2], outs[other][:2]):
+            assert np.array_equal(u, v)
 
 
 def test_independent_adapter_forward():
