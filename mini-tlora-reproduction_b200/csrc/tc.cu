@@ -42,6 +42,9 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
 
 #include "tc.cuh"
 
@@ -52,7 +55,6 @@ constexpr int kThreads = 192;
 constexpr int kBox64 = 64 * 64 * 2;  // one 64x64 bf16 box, 8 KB
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;
-constexpr int kGroupM = 8;           // raster group, in 256-row tiles
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kHalfRows = 128;       // rows of one CTA's A tile = TMEM lanes
 // 1-SM kernel: A 128x64 (16 KB) + B up to 256x64 (32 KB) per stage
@@ -82,6 +84,8 @@ struct TcParams {
   int n_tiles_rng;  // main: plan tiles of the launch
   int no_expand;    // main: leave the LoRA expand out
   int n_nblk;       // main: 256-wide N blocks
+  int raster_n;     // main: 0 = groups of M tiles sweep all N blocks, 1 = groups of N blocks sweep all M
+  int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
   const __nv_bfloat16* bias;
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
@@ -287,19 +291,33 @@ struct Item {
   bool skip;
 };
 
-// Main work item `item` over [tile0, tile0 + n_tiles_rng) x n_nblk, grouped
-// by kGroupM tiles so that concurrently running items share W tiles in L2.
+// Main work item `item` over [tile0, tile0 + n_tiles_rng) x n_nblk.  Items
+// are grouped so that the CTAs running at the same time share operand tiles
+// in L2: either a group of `group` M tiles sweeps every N block (the group's
+// A rows stay in L2 while W streams) or a group of `group` N blocks sweeps
+// every M tile (the group's W columns stay in L2 while A streams).  The host
+// picks the orientation and size with the least estimated DRAM traffic.
 // `units` = 1 (2-SM kernel: a unit is a 256-row tile) or 2 (1-SM kernel: a
 // unit is a 128-row half).
 __device__ __forceinline__ void raster(const TcParams& p, int item, int units, Item& it) {
   const int n_units = p.n_tiles_rng * units;
-  const int gm = kGroupM * units;
-  const int per_group = gm * p.n_nblk;
-  const int g = item / per_group, r = item % per_group;
-  const int u0 = g * gm;
-  const int gs = min(gm, n_units - u0);
-  it.nb = r / gs;
-  const int u = u0 + r % gs;
+  int u;
+  if (!p.raster_n) {
+    const int gm = p.group * units;
+    const int per_group = gm * p.n_nblk;
+    const int g = item / per_group, r = item % per_group;
+    const int u0 = g * gm;
+    const int gs = min(gm, n_units - u0);
+    it.nb = r / gs;
+    u = u0 + r % gs;
+  } else {
+    const int per_group = p.group * n_units;
+    const int g = item / per_group, r = item % per_group;
+    const int n0 = g * p.group;
+    const int gs = min(p.group, p.n_nblk - n0);
+    u = r / gs;
+    it.nb = n0 + r % gs;
+  }
   it.t = p.tile0 + u / units;
   it.half = u % units;
 }
@@ -894,6 +912,32 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
 }
 
+// Raster of a main launch with n_m 256-row tiles x n_n 256-wide N blocks and
+// K-extent k (bf16; A tiles and B blocks are both 256 x k).  Measured on B200
+// (c2 shapes, a sweep of orientations and group sizes on one box): the 1-SM
+// mainloop is fastest with groups of M tiles sweeping N, the 2-SM mainloop
+// with groups of N blocks sweeping M, both with about 48 MB of the
+// group's stationary operand (4..16 tiles or blocks).
+void choose_raster(TcParams& prm, bool pair, int n_m, int n_n, int k) {
+  const double tile = 256.0 * k * 2.0;
+  const int g = std::max(4, std::min(16, int(48.0 * (1 << 20) / tile + 0.5)));
+  prm.raster_n = pair ? 1 : 0;
+  prm.group = std::max(1, std::min(g, pair ? n_n : n_m));
+}
+
+// Tuning override of the raster from the environment: "m:<tiles>" or
+// "n:<blocks>" (e.g. MLORA_RASTER_FWD=m:8).  Returns false when unset.
+bool raster_override(const char* var, TcParams& prm) {
+  const char* v = std::getenv(var);
+  if (!v || !*v) return false;
+  char o = 0;
+  int g = 0;
+  if (std::sscanf(v, "%c:%d", &o, &g) != 2 || g < 1 || (o != 'm' && o != 'n')) return false;
+  prm.raster_n = o == 'n' ? 1 : 0;
+  prm.group = g;
+  return true;
+}
+
 TcParams base_params(const TcCall& a) {
   TcParams prm;
   memset(&prm, 0, sizeof(prm));
@@ -946,6 +990,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   prm.tile0 = a.t0;
   prm.n_tiles_rng = a.t1 - a.t0;
   prm.n_nblk = (a.d_out + 255) / 256;
+  if (!raster_override("MLORA_RASTER_FWD", prm)) choose_raster(prm, a.pair_fwd, prm.n_tiles_rng, prm.n_nblk, a.d_in);
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
@@ -981,6 +1026,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.tile0 = 0;
     prm.n_tiles_rng = a.plan.n_tiles;
     prm.n_nblk = (a.d_in + 255) / 256;
+    if (!raster_override("MLORA_RASTER_DX", prm)) choose_raster(prm, a.pair_dx, prm.n_tiles_rng, prm.n_nblk, a.d_out);
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
     if (!make_out_map(&prm.mY, a.dX, a.M, a.d_in)) return MLORA_ERR_UNSUPPORTED;

@@ -81,8 +81,12 @@ class NativeCompute:
     def main(self, ctx, t0, t1, expand, add_bias):
         ctx["fw"].main(t0, t1, expand=expand, add_bias=add_bias, max_ctas=self._main_ctas(ctx["fw"].x.device))
 
-    def backward(self, ctx, layer, x_p, dy):
-        return ops.backward_raw(dy, x_p, layer.W, ctx["fw"].z, ctx["st"], True, True, True)
+    def backward(self, ctx, layer, x_p, dy, overlapped=False):
+        st = ctx["st"]
+        if overlapped:  # leave SMs to the all-reduces still in flight
+            st = ops.LayerState(st.table, st.scaling, st.plan, st.A_pack, st.B_pack, st.impl,
+                                self._main_ctas(x_p.device))
+        return ops.backward_raw(dy, x_p, layer.W, ctx["fw"].z, st, True, True, True)
 
     def sgd(self, layer, plan, dA_p, dB, lr):
         pairs = []
@@ -116,8 +120,18 @@ class ShardedLayer:
         return x[:, self.k0:self.k1].contiguous()
 
     def forward(self, x_p, plan, n_nano: int, pipelined: bool = True, comm: bool = True):
-        """Pipelined forward; returns (Y, ctx).  ``comm=False`` skips the
-        collectives (compute-only timing)."""
+        """Pipelined forward; returns (Y, ctx) with every collective complete.
+        ``comm=False`` skips the collectives (compute-only timing)."""
+        y, ctx, works, hz = self.forward_async(x_p, plan, n_nano, pipelined, comm)
+        for w in works:
+            w.wait()
+        if hz is not None:
+            hz.wait()
+        return y, ctx
+
+    def forward_async(self, x_p, plan, n_nano: int, pipelined: bool = True, comm: bool = True):
+        """Pipelined forward that returns with the nano-batch all-reduces still
+        in flight: (Y, ctx, Y work handles, Z work handle or None)."""
         c = self.compute
         ctx = c.begin(self, x_p, plan)
         c.shrink(ctx)
@@ -139,21 +153,24 @@ class ShardedLayer:
                 works.append(dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
             else:
                 dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group)
-        for w in works:
-            w.wait()
-        if hz is not None:
-            hz.wait()
-        return ctx["y"], ctx
+        return ctx["y"], ctx, works, hz
 
-    def backward(self, ctx, x_p, dy):
-        return self.compute.backward(ctx, self, x_p, dy)
+    def backward(self, ctx, x_p, dy, overlapped=False):
+        return self.compute.backward(ctx, self, x_p, dy, overlapped)
 
     def step(self, x_p, plan, dy, n_nano: int, lr: float, pipelined: bool = True, comm: bool = True):
-        """Forward (pipelined all-reduce), backward and isolated SGD on this
-        rank's shard.  Returns (Y, dX_p)."""
-        y, ctx = self.forward(x_p, plan, n_nano, pipelined, comm)
-        dx_p, dA_p, dB = self.backward(ctx, x_p, dy)
+        """Forward, backward and isolated SGD on this rank's shard.  Returns
+        (Y, dX_p).  With ``pipelined`` the nano-batch all-reduces of Y overlap
+        the following nano-batches AND the backward: dY is the upstream
+        gradient, so the backward needs only the (small) all-reduced Z; the
+        Y all-reduces are waited for at the end of the step."""
+        y, ctx, works, hz = self.forward_async(x_p, plan, n_nano, pipelined, comm)
+        if hz is not None:
+            hz.wait()  # dB = dY^T Z needs the summed Z
+        dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works))
         self.compute.sgd(self, plan, dA_p, dB, lr)
+        for w in works:
+            w.wait()
         return y, dx_p
 
 
@@ -201,13 +218,13 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    # SMs the nano-batch mainloops leave to NCCL, and NCCL's channel (CTA)
-    # count matched to them so every channel of an all-reduce is resident
-    # while the next nano-batch computes; both fixed before the communicator
-    # exists, overridable from the environment
+    # SMs the mainloops leave to NCCL while all-reduces are in flight
+    # (MLORA_COMM_SMS), and optionally NCCL's channel (CTA) count
+    # (MLORA_NCCL_CHANNELS, fixed before the communicator exists)
     comm_sms = int(os.environ.get("MLORA_COMM_SMS", "16"))
-    os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, comm_sms)))
-    os.environ.setdefault("NCCL_MIN_NCHANNELS", str(max(1, comm_sms)))
+    if os.environ.get("MLORA_NCCL_CHANNELS"):
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", os.environ["MLORA_NCCL_CHANNELS"])
+        os.environ.setdefault("NCCL_MIN_NCHANNELS", os.environ["MLORA_NCCL_CHANNELS"])
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
         sp = workloads.spec(args.workload)
@@ -258,19 +275,40 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
         ms = _timed(stepper(best_n), args.steps, dev)
         launches = _lib.launch_count() - launches0
 
-        # end to end: pinned host shard of X, H2D inside the step, D2H probe
+        # end to end: every step copies its X shard from pinned host memory
+        # (copy stream, double-buffered: step i+1's copy overlaps step i) and
+        # reads a probe of the updated adapter weights back to the host
         x_host = x_p.detach().cpu().pin_memory()
-        x_dev = torch.empty_like(x_p)
+        bufs = [torch.empty_like(x_p) for _ in range(2)]
+        copied = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]
+        copy_stream = torch.cuda.Stream(dev)
+        compute = torch.cuda.current_stream(dev)
         probe = torch.empty(64, dtype=x_p.dtype).pin_memory()
+        counter = [0]
+
+        def issue_copy(i):
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(consumed[i % 2])
+                bufs[i % 2].copy_(x_host, non_blocking=True)
+                copied[i % 2].record(copy_stream)
 
         def e2e():
-            x_dev.copy_(x_host, non_blocking=True)
-            layer.step(x_dev, plan, dy, best_n, lr)
+            i = counter[0]
+            counter[0] += 1
+            compute.wait_event(copied[i % 2])
+            issue_copy(i + 1)
+            layer.step(bufs[i % 2], plan, dy, best_n, lr)
+            consumed[i % 2].record(compute)
             probe.copy_(layer.A_pack[0, :64], non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
+            compute.synchronize()
 
+        for ev in consumed:
+            ev.record(compute)
+        issue_copy(0)
         e2e()
         e2e_ms = _timed(e2e, max(3, args.steps // 2), dev)
+        torch.cuda.synchronize(dev)
 
         if rank != 0:
             return None

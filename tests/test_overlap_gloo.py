@@ -58,7 +58,7 @@ class DenseCompute:
             v = v + L.bias
         ctx["y"][r0:r1] = v
 
-    def backward(self, ctx, layer, x_p, dy):
+    def backward(self, ctx, layer, x_p, dy, overlapped=False):
         dz = (dy @ layer.B_pack) * ctx["mask"]
         dx = dy @ layer.W + dz @ layer.A_pack
         return dx, dz.T @ x_p, dy.T @ ctx["z"]
