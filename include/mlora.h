@@ -162,6 +162,27 @@ int mlora_backward(const mlora_problem* prob, const mlora_routing* route,
                    void* dX, void* dA_pack, void* dB_pack,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Stages of mlora_backward_staged. */
+#define MLORA_BWD_DZ 1  /* dZ = rowmask(s dY B) for plan tiles [tile_begin, tile_end) into dzsave;
+                           blocks of other tiles are not written */
+#define MLORA_BWD_DX 2  /* dX = dY W + dZ A over all rows (reads all of dzsave) */
+#define MLORA_BWD_DA 4  /* dA_pack = dZ^T X (reads all of dzsave) */
+#define MLORA_BWD_DB 8  /* dB_pack = dY^T Z for d_out rows [128 db_begin, 128 db_end) */
+
+/* mlora_backward split into stages and ranges, with the dZ intermediate in a
+ * caller-owned buffer dzsave (mlora_zsave_bytes bytes).  A K-sharded rank
+ * computes dZ for its share of the tiles and dB for its share of d_out, and
+ * sums dzsave / dB_pack across ranks between the stages
+ * (phase6_two_gpu_overlap.py:247-280 generalised to the backward).
+ * mlora_backward = all four stages over all tiles and all of d_out. */
+int mlora_backward_staged(const mlora_problem* prob, const mlora_routing* route,
+                          const void* dY, const void* X, const void* W,
+                          const void* A_pack, const void* B_pack, const void* zsave, void* dzsave,
+                          void* dX, void* dA_pack, void* dB_pack,
+                          void* workspace, size_t workspace_bytes, int32_t stages,
+                          int32_t tile_begin, int32_t tile_end, int32_t db_begin, int32_t db_end,
+                          void* stream);
+
 /* One parameter tensor of one adapter for mlora_sgd: a 2-D strided view
  * P[i * ld_param + j] (i < rows, j < cols) with gradient G[i * ld_grad + j]. */
 typedef struct mlora_sgd_item {

@@ -149,17 +149,29 @@ extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* rou
                               mlora_num_tiles(prob->rows), stream);
 }
 
-extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* route, const void* dY,
-                              const void* X, const void* W, const void* A_pack, const void* B_pack,
-                              const void* zsave, void* dX, void* dA_pack, void* dB_pack,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_routing* route,
+                                     const void* dY, const void* X, const void* W, const void* A_pack,
+                                     const void* B_pack, const void* zsave, void* dzsave, void* dX,
+                                     void* dA_pack, void* dB_pack, void* workspace, size_t workspace_bytes,
+                                     int32_t stages, int32_t tile_begin, int32_t tile_end, int32_t db_begin,
+                                     int32_t db_end, void* stream) {
   thread_local Plan p;
   int st = build_plan(prob, route, &p);
   if (st != MLORA_OK) return st;
+  if (stages & ~(MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB)) return MLORA_ERR_INVALID_ARG;
+  const int nb_out = (prob->d_out + 127) / 128;
+  if (tile_begin < 0 || tile_end < tile_begin || tile_end > p.n_tiles) return MLORA_ERR_INVALID_ARG;
+  if (db_begin < 0 || db_end < db_begin || db_end > nb_out) return MLORA_ERR_INVALID_ARG;
   if (prob->rows == 0) return MLORA_OK;
   if (!dY || !workspace) return MLORA_ERR_INVALID_ARG;
-  if (!p.chunks.empty() && (!A_pack || !B_pack || !zsave)) return MLORA_ERR_INVALID_ARG;
-  if ((dA_pack || dB_pack) && !X) return MLORA_ERR_INVALID_ARG;
+  const bool lora = !p.chunks.empty();
+  const bool need_dz = lora && ((stages & MLORA_BWD_DZ) || (dX && (stages & MLORA_BWD_DX)) ||
+                                (dA_pack && (stages & MLORA_BWD_DA)));
+  if (need_dz && (!dzsave || !B_pack)) return MLORA_ERR_INVALID_ARG;
+  if (lora && dX && (stages & MLORA_BWD_DX) && !A_pack) return MLORA_ERR_INVALID_ARG;
+  if (lora && dB_pack && (stages & MLORA_BWD_DB) && !zsave) return MLORA_ERR_INVALID_ARG;
+  if (((dA_pack && (stages & MLORA_BWD_DA)) || (dB_pack && (stages & MLORA_BWD_DB))) && !X)
+    return MLORA_ERR_INVALID_ARG;
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
   const int impl = choose_impl(prob);
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
@@ -167,16 +179,16 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
   PlanDev dev;
   st = upload_plan(p, workspace, s, &dev);
   if (st != MLORA_OK) return st;
-  void* dzt = (uint8_t*)workspace + align_up(p.bytes, 1024);
   if (impl == MLORA_IMPL_TC) {
     TcCall a;
     a.plan = dev;
     a.host = &p;
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
     a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
-    a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+    a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
     a.max_ctas = prob->max_ctas;
     a.pair_dx = prob->impl != MLORA_IMPL_TC_1SM;
+    a.bwd_stages = stages; a.t0 = tile_begin; a.t1 = tile_end; a.db0 = db_begin; a.db1 = db_end;
     return tc_backward(a, s);
   }
   SimtCall a;
@@ -186,8 +198,31 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
   a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
   a.dtype = prob->dtype;
   a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
-  a.zsave = (void*)zsave; a.dzt = dzt; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+  a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+  a.bwd_stages = stages; a.db0 = db_begin; a.db1 = db_end;
+  a.c_begin = p.tile_chunk_begin[tile_begin];
+  a.c_end = p.tile_chunk_begin[tile_end];
   return simt_backward(a, s);
+}
+
+extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* route, const void* dY,
+                              const void* X, const void* W, const void* A_pack, const void* B_pack,
+                              const void* zsave, void* dX, void* dA_pack, void* dB_pack,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!prob || !route) return MLORA_ERR_INVALID_ARG;
+  size_t plan_bytes = 0;
+  {
+    Plan p;
+    int st = build_plan(prob, route, &p);
+    if (st != MLORA_OK) return st;
+    plan_bytes = p.bytes;
+  }
+  // dZ scratch lives in the workspace after the plan tables
+  void* dzt = workspace ? (uint8_t*)workspace + align_up(plan_bytes, 1024) : nullptr;
+  return mlora_backward_staged(prob, route, dY, X, W, A_pack, B_pack, zsave, dzt, dX, dA_pack, dB_pack,
+                               workspace, workspace_bytes,
+                               ((dX || dA_pack) ? MLORA_BWD_DZ : 0) | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB, 0,
+                               mlora_num_tiles(prob->rows), 0, (prob->d_out + 127) / 128, stream);
 }
 
 extern "C" int mlora_sgd(const mlora_sgd_item* items, int32_t n_items, float lr, int32_t dtype,

@@ -167,14 +167,14 @@ __global__ void __launch_bounds__(NT) k_reduce(PlanDev plan, const T* __restrict
                                                 const T* __restrict__ dY, const T* __restrict__ zt,
                                                 const T* __restrict__ dzt, T* __restrict__ dA,
                                                 T* __restrict__ dB, int64_t M, int d_in, int d_out,
-                                                int R) {
+                                                int R, int db0, int db1) {
   __shared__ float As[BK][LD], Bs[BK][LD];
   const ReduceItem it = plan.reduce[blockIdx.x];
   const int jc = blockIdx.y;
   if (jc >= it.nc) return;
   const int j = it.j0 + jc;
   const bool is_dB = it.kind == 1;
-  if ((is_dB && !dB) || (!is_dB && !dA)) return;
+  if ((is_dB && (!dB || it.block < db0 || it.block >= db1)) || (!is_dB && !dA)) return;
   const int D = is_dB ? d_out : d_in;
   const int b0 = it.block * 128 + blockIdx.z * BM;
   if (b0 >= D) return;
@@ -254,22 +254,24 @@ int launch_forward(const SimtCall& a, cudaStream_t st) {
 
 template <class T>
 int launch_backward(const SimtCall& a, cudaStream_t st) {
-  if (a.n_chunks > 0 && (a.dX || a.dA)) {
-    k_shrink<T, true><<<dim3(a.n_chunks, kTileRows / BM), NT, 0, st>>>(
-        a.plan, (const T*)a.dY, (const T*)a.B_pack, (T*)a.dzt, a.M, a.d_in, a.d_out, a.R, 0);
+  if ((a.bwd_stages & MLORA_BWD_DZ) && a.c_end > a.c_begin) {
+    k_shrink<T, true><<<dim3(a.c_end - a.c_begin, kTileRows / BM), NT, 0, st>>>(
+        a.plan, (const T*)a.dY, (const T*)a.B_pack, (T*)a.dzt, a.M, a.d_in, a.d_out, a.R, a.c_begin);
     count_launch();
   }
-  if (a.dX && a.M > 0) {
+  if (a.dX && (a.bwd_stages & MLORA_BWD_DX) && a.M > 0) {
     dim3 grid((a.d_in + BN - 1) / BN, unsigned((a.M + BM - 1) / BM));
     k_main<T, true><<<grid, NT, 0, st>>>(a.plan, (const T*)a.dY, (const T*)a.W, nullptr,
                                          (const T*)a.A_pack, (const T*)a.dzt, (T*)a.dX, a.M,
                                          a.d_in, a.d_out, a.R, 0, 0);
     count_launch();
   }
-  if (a.n_reduce > 0 && (a.dA || a.dB)) {
+  void* dA = (a.bwd_stages & MLORA_BWD_DA) ? a.dA : nullptr;
+  void* dB = (a.bwd_stages & MLORA_BWD_DB) && a.db1 > a.db0 ? a.dB : nullptr;
+  if (a.n_reduce > 0 && (dA || dB)) {
     k_reduce<T><<<dim3(a.n_reduce, kMaxChunksPerItem, 2), NT, 0, st>>>(
-        a.plan, (const T*)a.X, (const T*)a.dY, (const T*)a.zsave, (const T*)a.dzt, (T*)a.dA,
-        (T*)a.dB, a.M, a.d_in, a.d_out, a.R);
+        a.plan, (const T*)a.X, (const T*)a.dY, (const T*)a.zsave, (const T*)a.dzt, (T*)dA,
+        (T*)dB, a.M, a.d_in, a.d_out, a.R, a.db0, a.db1);
     count_launch();
   }
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;

@@ -20,6 +20,9 @@ struct SimtCall {
   // forward stages (MLORA_STAGE_*), plan tile range [t0, t1) and its chunk range
   int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
   int t0 = 0, t1 = 0, c_begin = 0, c_end = 0;
+  // backward stages (MLORA_BWD_*) and dB block range (128-row blocks of d_out)
+  int bwd_stages = MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB;
+  int db0 = 0, db1 = 0;
 };
 
 int simt_forward(const SimtCall& a, cudaStream_t st);

@@ -87,6 +87,8 @@ struct TcParams {
   int raster_n;     // main: 0 = groups of M tiles sweep all N blocks, 1 = groups of N blocks sweep all M
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
+  int da_on;        // reduce: compute dA items
+  int db0, db1;     // reduce: dB items of d_out blocks [db0, db1)
   const __nv_bfloat16* bias;
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
   __nv_bfloat16* dA;
@@ -350,7 +352,8 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
     it.n = 64 * it.nc;
     it.t = 0;
     it.c0 = 0;
-    it.skip = it.ri.kind == 0 ? (p.dA == nullptr) : (p.dB == nullptr);
+    it.skip = it.ri.kind == 0 ? (p.dA == nullptr || !p.da_on)
+                              : (p.dB == nullptr || it.ri.block < p.db0 || it.ri.block >= p.db1);
   }
   return it;
 }
@@ -1007,16 +1010,20 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
   const int64_t zrows = int64_t(n_chunks) * kTileRows;
   int s;
-  if (n_chunks > 0 && (a.dX || a.dA)) {
+  if (n_chunks > 0 && (a.bwd_stages & MLORA_BWD_DZ) && a.t1 > a.t0) {
+    const std::vector<ShrinkItem>& sh = a.host->shrink;
+    auto lo = std::lower_bound(sh.begin(), sh.end(), a.t0, [](const ShrinkItem& v, int t) { return v.tile < t; });
+    auto hi = std::lower_bound(sh.begin(), sh.end(), a.t1, [](const ShrinkItem& v, int t) { return v.tile < t; });
     TcParams prm = base_params(a);
     if (!make_map(&prm.mA0, a.dY, a.M, a.d_out, 128) || !make_map(&prm.mB0, a.B_pack, a.d_out, a.R, 64))
       return MLORA_ERR_UNSUPPORTED;
-    prm.n_items = 2 * a.plan.n_shrink;
+    prm.item0 = int(lo - sh.begin());
+    prm.n_items = 2 * int(hi - lo);
     prm.nk_main = (a.d_out + 63) / 64;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
     if ((s = launch1<SHRINK_BWD>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
-  if (a.dX) {
+  if (a.dX && (a.bwd_stages & MLORA_BWD_DX)) {
     TcParams prm = base_params(a);
     if (!make_map(&prm.mA0, a.dY, a.M, a.d_out, 128) || (a.W && !make_map(&prm.mB0, a.W, a.d_out, a.d_in, 64)))
       return MLORA_ERR_UNSUPPORTED;
@@ -1039,7 +1046,9 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     }
     if (s != MLORA_OK) return s;
   }
-  if (n_chunks > 0 && (a.dA || a.dB)) {
+  const bool da = a.dA && (a.bwd_stages & MLORA_BWD_DA);
+  const bool db = a.dB && (a.bwd_stages & MLORA_BWD_DB) && a.db1 > a.db0;
+  if (n_chunks > 0 && (da || db)) {
     TcParams prm = base_params(a);
     if (!make_map(&prm.mA0, a.X, a.M, a.d_in, 64) || !make_map(&prm.mB0, a.dzt, zrows, 64, 64) ||
         !make_map(&prm.mA1, a.dY, a.M, a.d_out, 64) || !make_map(&prm.mB1, a.zsave, zrows, 64, 64))
@@ -1047,6 +1056,9 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.n_items = a.plan.n_reduce;
     prm.dA = reinterpret_cast<__nv_bfloat16*>(a.dA);
     prm.dB = reinterpret_cast<__nv_bfloat16*>(a.dB);
+    prm.da_on = da ? 1 : 0;
+    prm.db0 = db ? a.db0 : 0;
+    prm.db1 = db ? a.db1 : 0;
     if ((s = launch1<REDUCE>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
   return MLORA_OK;

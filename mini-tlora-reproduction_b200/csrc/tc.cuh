@@ -21,6 +21,9 @@ struct TcCall {
   int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
   int t0 = 0, t1 = 0;
   int max_ctas = 0;  // 0 = one CTA per SM
+  // backward stages (MLORA_BWD_*), dZ tile range [t0, t1) and dB block range
+  int bwd_stages = MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB;
+  int db0 = 0, db1 = 0;
   bool pair_fwd = false;  // forward mainloop on 2-SM pairs (tcgen05 cta_group::2)
   bool pair_dx = true;    // dX mainloop on 2-SM pairs
 };

@@ -35,6 +35,11 @@ STAGE_SHRINK = 1
 STAGE_MAIN = 2
 STAGE_NO_EXPAND = 4
 
+BWD_DZ = 1
+BWD_DX = 2
+BWD_DA = 4
+BWD_DB = 8
+
 IMPL_AUTO = 0
 IMPL_SIMT = 1
 IMPL_TC = 2
@@ -95,6 +100,9 @@ SIGNATURES = {
                                              _VP, _VP, _VP]),
     "mlora_backward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,
                                       _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _VP]),
+    "mlora_backward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,
+                                             _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, ctypes.c_int32,
+                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VP]),
     "mlora_sgd": (ctypes.c_int, [ctypes.POINTER(SgdItem), ctypes.c_int32, ctypes.c_float, ctypes.c_int32, _VP]),
     "mlora_route_runs": (ctypes.c_int, [_VP, ctypes.c_int64, _VP, _VP, ctypes.c_int32, ctypes.c_int32, _VP, _VP]),
     "mlora_route_sort_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32]),

@@ -322,6 +322,55 @@ def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, wan
     return dx, dA, dB
 
 
+class StagedBackward:
+    """Backward of one routing plan split into stages and ranges: ``dz(t0,
+    t1)`` writes the dZ intermediate of tiles [t0, t1) into ``dz`` (a zeroed
+    caller-visible buffer, so partial results of several ranks can be
+    summed); ``dx()``, ``da()`` and ``db(b0, b1)`` (128-row blocks of d_out)
+    read it.  ``dB`` starts at zero so that blocks computed elsewhere can be
+    summed in."""
+
+    def __init__(self, dy, xs, W, z, st: LayerState):
+        self.dy, self.xs, self.W, self.z, self.st = dy, xs, W, z, st
+        rows = dy.shape[0]
+        d_in = st.A_pack.shape[1]
+        d_out = st.B_pack.shape[0]
+        dev = dy.device
+        self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
+                              st.max_ctas)
+        zb, wb = self.args.sizes()
+        self.ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+        self.wb = wb
+        self.dz_bytes = zb
+        self.dz = torch.zeros(max(zb, 1), dtype=torch.uint8, device=dev)
+        self.dx = torch.empty(rows, d_in, dtype=dy.dtype, device=dev)
+        self.dA = torch.zeros_like(st.A_pack)
+        self.dB = torch.zeros_like(st.B_pack)
+        self.n_tiles = int(_lib.lib().mlora_num_tiles(rows))
+        self.n_db = (d_out + 127) // 128
+
+    def dz_view(self):
+        return self.dz[:self.dz_bytes].view(self.dy.dtype) if self.dz_bytes else None
+
+    def _run(self, stages, t0=0, t1=0, b0=0, b1=0):
+        _lib.call("mlora_backward_staged", ctypes.byref(self.args.prob), ctypes.byref(self.args.route),
+                  _ptr(self.dy), _ptr(self.xs), _ptr(self.W), _ptr(self.st.A_pack), _ptr(self.st.B_pack),
+                  _ptr(self.z), _ptr(self.dz), _ptr(self.dx), _ptr(self.dA), _ptr(self.dB), _ptr(self.ws), self.wb,
+                  stages, t0, t1, b0, b1, _stream(self.dy.device))
+
+    def run_dz(self, t0=0, t1=None):
+        self._run(_lib.BWD_DZ, t0, self.n_tiles if t1 is None else t1)
+
+    def run_dx(self):
+        self._run(_lib.BWD_DX)
+
+    def run_da(self):
+        self._run(_lib.BWD_DA)
+
+    def run_db(self, b0=0, b1=None):
+        self._run(_lib.BWD_DB, 0, 0, b0, self.n_db if b1 is None else b1)
+
+
 class MultiLoRAFunction(torch.autograd.Function):
     """Y = X W^T + b + per-segment LoRA, with the analytic backward.
 

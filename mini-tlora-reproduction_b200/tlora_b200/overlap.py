@@ -50,6 +50,15 @@ def shard_columns(d_in: int, rank: int, world: int, align: int = 64) -> Tuple[in
     return min(d_in, s * align), min(d_in, e * align)
 
 
+def _share(total: int, rank: int, world: int) -> Tuple[int, int]:
+    """Rank ``rank``'s contiguous share of ``total`` items (empty when there
+    are fewer items than ranks and this rank gets none)."""
+    if total <= 0:
+        return 0, 0
+    spans = split_ranges(total, world)
+    return spans[rank] if rank < len(spans) else (total, total)
+
+
 class NativeCompute:
     """The native kernels (tcgen05 for bf16) behind the sharded layer.
     ``comm_sms`` SMs are left out of the nano-batch mainloops so the NCCL
@@ -81,12 +90,24 @@ class NativeCompute:
     def main(self, ctx, t0, t1, expand, add_bias):
         ctx["fw"].main(t0, t1, expand=expand, add_bias=add_bias, max_ctas=self._main_ctas(ctx["fw"].x.device))
 
-    def backward(self, ctx, layer, x_p, dy, overlapped=False):
+    def bwd_begin(self, ctx, layer, x_p, dy, overlapped=False):
         st = ctx["st"]
         if overlapped:  # leave SMs to the all-reduces still in flight
             st = ops.LayerState(st.table, st.scaling, st.plan, st.A_pack, st.B_pack, st.impl,
                                 self._main_ctas(x_p.device))
-        return ops.backward_raw(dy, x_p, layer.W, ctx["fw"].z, st, True, True, True)
+        bw = ops.StagedBackward(dy, x_p, layer.W, ctx["fw"].z, st)
+        return {"bw": bw, "dz": bw.dz_view(), "dx": bw.dx, "dA": bw.dA, "dB": bw.dB,
+                "n_tiles": bw.n_tiles, "n_db": bw.n_db}
+
+    def bwd_dz(self, b, t0, t1):
+        b["bw"].run_dz(t0, t1)
+
+    def bwd_dx_da(self, b):
+        b["bw"].run_dx()
+        b["bw"].run_da()
+
+    def bwd_db(self, b, b0, b1):
+        b["bw"].run_db(b0, b1)
 
     def sgd(self, layer, plan, dA_p, dB, lr):
         pairs = []
@@ -156,7 +177,22 @@ class ShardedLayer:
         return ctx["y"], ctx, works, hz
 
     def backward(self, ctx, x_p, dy, overlapped=False):
-        return self.compute.backward(ctx, self, x_p, dy, overlapped)
+        """Backward on this rank's shard.  dZ (needs all of dY and B) and dB
+        (needs all of dY and Z) are split across ranks — dZ by tiles, dB by
+        128-row blocks of d_out — and summed with two small all-reduces;
+        dX_p and dA_p are local.  Returns (dX_p, dA_p, dB)."""
+        c = self.compute
+        b = c.bwd_begin(ctx, self, x_p, dy, overlapped)
+        t0, t1 = _share(b["n_tiles"], self.rank, self.world)
+        c.bwd_dz(b, t0, t1)
+        if b["dz"] is not None and self.world > 1:
+            dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.group)
+        c.bwd_dx_da(b)
+        b0, b1 = _share(b["n_db"], self.rank, self.world)
+        c.bwd_db(b, b0, b1)
+        if self.world > 1:
+            dist.all_reduce(b["dB"], op=dist.ReduceOp.SUM, group=self.group)
+        return b["dx"], b["dA"], b["dB"]
 
     def step(self, x_p, plan, dy, n_nano: int, lr: float, pipelined: bool = True, comm: bool = True):
         """Forward, backward and isolated SGD on this rank's shard.  Returns
@@ -207,10 +243,83 @@ def _timed(fn, iters: int, device) -> float:
     return float(t.item())
 
 
-def bench_multi(args, peaks_d, peaks_kind, metric, unit):
-    import datetime
-
+def _job_parallel(args, rank, world, dev, metric, unit):
+    """Weak scaling without any collective on the data path: every rank trains
+    its own set of jobs (same layer shape, its own adapters and rows, seeded
+    by rank) on its own replica of the frozen backbone.  Returns the per-step
+    device time (max over ranks) of the timed region and the e2e time."""
     from . import _lib, workloads
+    from .nano import AIMDController  # noqa: F401  (kept for symmetry of imports)
+
+    sp = workloads.spec(args.workload, rows_scale=getattr(args, "rows_scale", 1.0))
+    sp.seed = sp.seed + 7919 * rank
+    w = workloads.build(sp, device=dev)
+    m = w.model
+    x = w.x.requires_grad_(True)
+    ids_host = w.ids.cpu()
+
+    def step(xi=None):
+        for ad in m.adapters.values():
+            ad.A.grad = None
+            ad.B.grad = None
+        xx = x if xi is None else xi
+        xx.grad = None
+        y = m(xx, ids_host)
+        y.backward(w.dy)
+        m.sgd_step(sp.lr)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    launches0 = _lib.launch_count()
+    ms = _timed(step, args.steps, dev)
+    launches = _lib.launch_count() - launches0
+    # e2e: prefetched pinned H2D of this rank's X, probe read back every step
+    x_host = w.x.detach().cpu().pin_memory()
+    bufs = [torch.empty_like(w.x.detach()) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    copy_stream = torch.cuda.Stream(dev)
+    compute = torch.cuda.current_stream(dev)
+    probe = torch.empty(64, dtype=w.x.dtype).pin_memory()
+    a0 = m.adapters["0"].A
+    counter = [0]
+
+    def issue_copy(i):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(consumed[i % 2])
+            bufs[i % 2].copy_(x_host, non_blocking=True)
+            copied[i % 2].record(copy_stream)
+
+    def e2e():
+        i = counter[0]
+        counter[0] += 1
+        compute.wait_event(copied[i % 2])
+        issue_copy(i + 1)
+        step(bufs[i % 2].detach().requires_grad_(True))
+        consumed[i % 2].record(compute)
+        probe.copy_(a0.detach()[0, :64], non_blocking=True)
+        compute.synchronize()
+
+    for ev in consumed:
+        ev.record(compute)
+    issue_copy(0)
+    e2e()
+    e2e_ms = _timed(e2e, max(3, args.steps // 2), dev)
+    torch.cuda.synchronize(dev)
+    out = {"sp": sp, "ms": ms, "e2e_ms": e2e_ms, "launches": launches,
+           "h2d": int(w.x.numel() * w.x.element_size()), "d2h": int(probe.numel() * probe.element_size())}
+    del w, m, x, bufs
+    torch.cuda.empty_cache()
+    return out
+
+
+def bench_multi(args, peaks_d, peaks_kind, metric, unit):
+    """bench.py --gpus N (N > 1).  Primary value: job-parallel weak scaling
+    (the jobs are independent and the backbone is frozen, so no collective
+    is needed).  Also measured in the same run and reported as `ksharded`:
+    one layer K-sharded across the ranks with the nano-batch all-reduce
+    overlap steered by AIMD (the rebuilt phase6 pipeline)."""
+    import datetime
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -218,123 +327,96 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    # SMs the mainloops leave to NCCL while all-reduces are in flight
-    # (MLORA_COMM_SMS), and optionally NCCL's channel (CTA) count
-    # (MLORA_NCCL_CHANNELS, fixed before the communicator exists)
     comm_sms = int(os.environ.get("MLORA_COMM_SMS", "16"))
     if os.environ.get("MLORA_NCCL_CHANNELS"):
         os.environ.setdefault("NCCL_MAX_NCHANNELS", os.environ["MLORA_NCCL_CHANNELS"])
         os.environ.setdefault("NCCL_MIN_NCHANNELS", os.environ["MLORA_NCCL_CHANNELS"])
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
-        sp = workloads.spec(args.workload)
-        w = workloads.build(sp, device=dev)
-        layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms))
-        x_p = layer.shard_input(w.x)
-        plan = ops.route(w.ids, layer.table, dev)
-        lr = sp.lr
-        dy = w.dy
-        n_tiles = (sp.rows + TILE_ROWS - 1) // TILE_ROWS
-
-        def stepper(n, pipelined=True, comm=True):
-            return lambda: layer.step(x_p, plan, dy, n, lr, pipelined, comm)
-
-        for _ in range(max(3, args.warmup)):
-            stepper(4)()
-        torch.cuda.synchronize(dev)
-
-        # AIMD over the real pipelined step (phase6b_real_aimd.py:245-302)
-        ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
-        horizons = []
-        for _ in range(8):
-            n = ctl.n
-            t = _timed(stepper(n), 3, dev)
-            nxt, why = ctl.observe(t)
-            horizons.append({"n": n, "ms": round(t, 4), "decision": why, "next_n": nxt})
-        best_n = ctl.best_n
-
-        # SMs left to NCCL during the nano-batch mainloops (the persistent
-        # mainloop would otherwise hold every SM and serialise the all-reduce)
-        sm_sweep = {}
-        for k in sorted({0, comm_sms // 2, comm_sms, comm_sms + comm_sms // 2}):
-            layer.compute.comm_sms = k
-            sm_sweep[k] = _timed(stepper(best_n), 3, dev)
-        best_k = min(sm_sweep, key=sm_sweep.get)
-        layer.compute.comm_sms = best_k
-
-        # overlap accounting at the chosen N
-        t_pipe = _timed(stepper(best_n), 3, dev)
-        t_serial = _timed(stepper(best_n, pipelined=False), 3, dev)
-        t_compute = _timed(stepper(best_n, comm=False), 3, dev)
-        y_buf, ctx = layer.forward(x_p, plan, best_n)
-        t_comm = _timed(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
-        hidden = 1.0 - max(0.0, t_pipe - t_compute) / t_comm if t_comm > 0 else 0.0
-
-        # timed region
-        launches0 = _lib.launch_count()
-        ms = _timed(stepper(best_n), args.steps, dev)
-        launches = _lib.launch_count() - launches0
-
-        # end to end: every step copies its X shard from pinned host memory
-        # (copy stream, double-buffered: step i+1's copy overlaps step i) and
-        # reads a probe of the updated adapter weights back to the host
-        x_host = x_p.detach().cpu().pin_memory()
-        bufs = [torch.empty_like(x_p) for _ in range(2)]
-        copied = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]
-        copy_stream = torch.cuda.Stream(dev)
-        compute = torch.cuda.current_stream(dev)
-        probe = torch.empty(64, dtype=x_p.dtype).pin_memory()
-        counter = [0]
-
-        def issue_copy(i):
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(consumed[i % 2])
-                bufs[i % 2].copy_(x_host, non_blocking=True)
-                copied[i % 2].record(copy_stream)
-
-        def e2e():
-            i = counter[0]
-            counter[0] += 1
-            compute.wait_event(copied[i % 2])
-            issue_copy(i + 1)
-            layer.step(bufs[i % 2], plan, dy, best_n, lr)
-            consumed[i % 2].record(compute)
-            probe.copy_(layer.A_pack[0, :64], non_blocking=True)
-            compute.synchronize()
-
-        for ev in consumed:
-            ev.record(compute)
-        issue_copy(0)
-        e2e()
-        e2e_ms = _timed(e2e, max(3, args.steps // 2), dev)
-        torch.cuda.synchronize(dev)
-
+        jp = _job_parallel(args, rank, world, dev, metric, unit)
+        ks = _ksharded(args, rank, world, dev, comm_sms)
         if rank != 0:
             return None
-        step_flops = sp.flops()
+        sp = jp["sp"]
+        ms = jp["ms"]
+        step_flops = sp.flops() * world
         return {
-            "metric": metric, "value": round(sp.rows / (ms / 1000.0), 1), "unit": unit, "n_gpus": world,
+            "metric": metric, "value": round(world * sp.rows / (ms / 1000.0), 1), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded; random-init weights)",
-            "config": {"workload": f"{sp.name}: fwd+bwd+isolated SGD d_in={sp.d_in} d_out={sp.d_out}, "
-                                   f"backbone K-sharded over {world} GPUs, nano-batch all-reduce overlap",
-                       "rows": sp.rows, "global_batch": sp.rows, "seq_len": None,
-                       "parallelism": f"K-shard x{world} + nano-batch pipeline (AIMD N={best_n})",
-                       "l2": "per-step traffic (Y all-reduce, 1.4 GiB) larger than L2"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded per rank; random-init weights)",
+            "config": {"workload": f"{sp.name}: fwd+bwd+isolated SGD d_in={sp.d_in} d_out={sp.d_out} per GPU, "
+                                   "job-parallel (each GPU trains its own adapters on a frozen-backbone replica)",
+                       "rows": sp.rows * world, "global_batch": sp.rows * world, "seq_len": None,
+                       "parallelism": f"job-parallel x{world} (no collective on the data path)",
+                       "l2": "inputs larger than L2 (X 512 MiB per GPU)"},
             "step_tflops": round(step_flops / (ms / 1000.0) / 1e12, 1),
+            "e2e": {"value": round(world * sp.rows / (jp["e2e_ms"] / 1000.0), 1), "unit": unit,
+                    "ms_per_step": round(jp["e2e_ms"], 3), "h2d_bytes_per_step": jp["h2d"] * world,
+                    "d2h_bytes_per_step": jp["d2h"] * world},
+            "gpu_launches": int(jp["launches"]),
+            "ksharded": ks,
+        }
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _ksharded(args, rank, world, dev, comm_sms):
+    """The K-sharded layer with the nano-batch all-reduce pipeline: AIMD over
+    the nano-batch count, the SM reservation sweep, overlap accounting, timed
+    steps and the prefetched e2e loop.  Returns the summary (rank 0)."""
+    from . import _lib, workloads
+
+    sp = workloads.spec(args.workload, rows_scale=getattr(args, "rows_scale", 1.0))
+    w = workloads.build(sp, device=dev)
+    layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms))
+    x_p = layer.shard_input(w.x)
+    plan = ops.route(w.ids.cpu(), layer.table, dev)
+    lr = sp.lr
+    dy = w.dy
+    n_tiles = (sp.rows + TILE_ROWS - 1) // TILE_ROWS
+
+    def stepper(n, pipelined=True, comm=True):
+        return lambda: layer.step(x_p, plan, dy, n, lr, pipelined, comm)
+
+    for _ in range(max(3, args.warmup)):
+        stepper(4)()
+    torch.cuda.synchronize(dev)
+
+    # AIMD over the real pipelined step (phase6b_real_aimd.py:245-302)
+    ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
+    horizons = []
+    for _ in range(8):
+        n = ctl.n
+        t = _timed(stepper(n), 3, dev)
+        nxt, why = ctl.observe(t)
+        horizons.append({"n": n, "ms": round(t, 4), "decision": why, "next_n": nxt})
+    best_n = ctl.best_n
+
+    sm_sweep = {}
+    for k in sorted({0, comm_sms // 2, comm_sms, comm_sms + comm_sms // 2}):
+        layer.compute.comm_sms = k
+        sm_sweep[k] = _timed(stepper(best_n), 3, dev)
+    best_k = min(sm_sweep, key=sm_sweep.get)
+    layer.compute.comm_sms = best_k
+
+    t_pipe = _timed(stepper(best_n), 3, dev)
+    t_serial = _timed(stepper(best_n, pipelined=False), 3, dev)
+    t_compute = _timed(stepper(best_n, comm=False), 3, dev)
+    y_buf, ctx = layer.forward(x_p, plan, best_n)
+    t_comm = _timed(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
+    hidden = 1.0 - max(0.0, t_pipe - t_compute) / t_comm if t_comm > 0 else 0.0
+    ms = _timed(stepper(best_n), args.steps, dev)
+    del w
+    if rank != 0:
+        return None
+    return {"value": round(sp.rows / (ms / 1000.0), 1), "ms_per_step": round(ms, 4), "scaling": "strong",
+            "workload": f"{sp.name} one layer, backbone K-sharded over {world} GPUs",
+            "rows": sp.rows, "step_tflops": round(sp.flops() / (ms / 1000.0) / 1e12, 1),
             "overlap": {"n": best_n, "comm_sms": best_k, "nccl_channels": os.environ.get("NCCL_MAX_NCHANNELS"),
                         "comm_sms_sweep_ms": {str(k): round(v, 4) for k, v in sm_sweep.items()},
                         "pipelined_ms": round(t_pipe, 4), "serial_ms": round(t_serial, 4),
                         "compute_only_ms": round(t_compute, 4), "comm_only_ms": round(t_comm, 4),
                         "comm_hidden_frac": round(hidden, 4)},
-            "aimd": horizons,
-            "e2e": {"value": round(sp.rows / (e2e_ms / 1000.0), 1), "unit": unit, "ms_per_step": round(e2e_ms, 3),
-                    "h2d_bytes_per_step": int(x_p.numel() * x_p.element_size()),
-                    "d2h_bytes_per_step": int(probe.numel() * probe.element_size())},
-            "gpu_launches": int(launches),
-        }
-    finally:
-        dist.barrier()
-        dist.destroy_process_group()
+            "aimd": horizons}

@@ -240,3 +240,35 @@ def test_independent_adapter_forward():
 def test_no_device_error_word():
     from tlora_b200 import _lib
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc")])
+def test_staged_backward_matches_backward(dtype, impl):
+    """The staged backward (dZ by tile ranges, dB by d_out block ranges, as the
+    K-sharded ranks split it) pieces together exactly mlora_backward."""
+    from tlora_b200 import ops
+    m = _edge_module(256, 640, {0: 8, 1: 70, 2: 16}, dtype)
+    m.impl = impl
+    ids = torch.tensor([0] * 300 + [1] * 200 + [2] * 157, device=DEV)
+    x = torch.randn(ids.shape[0], 256, device=DEV).to(dtype)
+    dy = torch.randn(ids.shape[0], 640, device=DEV).to(dtype)
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(ids, table, torch.device(DEV))
+    st = ops.LayerState(table, np.array([float(a.scaling) for a in m.adapters.values()], np.float32), plan,
+                        A_pack, B_pack, impl)
+    _, z, xs, _ = ops.forward_raw(x, m.base.weight, m.base.bias, st)
+    dx, dA, dB = ops.backward_raw(dy, xs, m.base.weight, z, st, True, True, True)
+    bw = ops.StagedBackward(dy, xs, m.base.weight, z, st)
+    half_t = bw.n_tiles // 2
+    bw.run_dz(0, half_t)
+    bw.run_dz(half_t, bw.n_tiles)
+    bw.run_dx()
+    bw.run_da()
+    bw.run_db(0, 2)
+    bw.run_db(2, bw.n_db)
+    torch.cuda.synchronize()
+    assert torch.equal(bw.dx, dx)
+    for i in range(table.n):
+        o, r = int(table.pack_off[i]), int(table.rank[i])
+        assert torch.equal(bw.dA[o:o + r], dA[o:o + r])
+        assert torch.equal(bw.dB[:, o:o + r], dB[:, o:o + r])

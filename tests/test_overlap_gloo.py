@@ -58,10 +58,27 @@ class DenseCompute:
             v = v + L.bias
         ctx["y"][r0:r1] = v
 
-    def backward(self, ctx, layer, x_p, dy, overlapped=False):
-        dz = (dy @ layer.B_pack) * ctx["mask"]
-        dx = dy @ layer.W + dz @ layer.A_pack
-        return dx, dz.T @ x_p, dy.T @ ctx["z"]
+    def bwd_begin(self, ctx, layer, x_p, dy, overlapped=False):
+        rows = x_p.shape[0]
+        d_out = layer.B_pack.shape[0]
+        return {"ctx": ctx, "layer": layer, "x": x_p, "dy": dy,
+                "dz": torch.zeros(rows, layer.table.r_pack, dtype=torch.float64),
+                "dx": None, "dA": None, "dB": torch.zeros_like(layer.B_pack),
+                "n_tiles": (rows + TILE - 1) // TILE, "n_db": (d_out + 127) // 128}
+
+    def bwd_dz(self, b, t0, t1):
+        L, ctx = b["layer"], b["ctx"]
+        r0, r1 = t0 * TILE, min(t1 * TILE, b["x"].shape[0])
+        b["dz"][r0:r1] = (b["dy"][r0:r1] @ L.B_pack) * ctx["mask"][r0:r1]
+
+    def bwd_dx_da(self, b):
+        L = b["layer"]
+        b["dx"] = b["dy"] @ L.W + b["dz"] @ L.A_pack
+        b["dA"] = b["dz"].T @ b["x"]
+
+    def bwd_db(self, b, b0, b1):
+        r0, r1 = b0 * 128, min(b1 * 128, b["dB"].shape[0])
+        b["dB"][r0:r1] = b["dy"][:, r0:r1].T @ b["ctx"]["z"]
 
     def sgd(self, layer, plan, dA, dB, lr):
         for i in range(layer.table.n):
@@ -81,16 +98,16 @@ def _free_port():
 
 def _build(seed=0):
     torch.manual_seed(seed)
-    m = MultiLoRALinear(256, 96, {0: 4, 1: 70, 2: 8}).double()
+    m = MultiLoRALinear(256, 300, {0: 4, 1: 70, 2: 8}).double()
     with torch.no_grad():
         m.base.bias.normal_(0, 0.1)
         for ad in m.adapters.values():
             ad.B.normal_(0, 0.05)
             ad.scaling = 2.0
-    ids = torch.tensor([0] * 150 + [1] * 100 + [2] * 77 + [9] * 5)
+    ids = torch.tensor([0] * 300 + [1] * 200 + [2] * 77 + [9] * 5)
     g = torch.Generator().manual_seed(seed + 1)
     x = torch.randn(ids.shape[0], 256, generator=g, dtype=torch.float64)
-    dy = torch.randn(ids.shape[0], 96, generator=g, dtype=torch.float64)
+    dy = torch.randn(ids.shape[0], 300, generator=g, dtype=torch.float64)
     return m, ids, x, dy
 
 
