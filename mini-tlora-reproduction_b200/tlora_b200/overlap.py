@@ -123,8 +123,12 @@ class NativeCompute:
 class ShardedLayer:
     """Rank ``rank``'s K-shard of a MultiLoRALinear (see module docstring)."""
 
-    def __init__(self, model, rank: int, world: int, compute=None, group=None):
+    def __init__(self, model, rank: int, world: int, compute=None, group=None, bwd_group=None):
+        # `bwd_group`: a second communicator for the backward's small
+        # all-reduces (dZ, dB), so they do not queue behind the large Y
+        # all-reduces still in flight on `group`
         self.rank, self.world, self.group = rank, world, group
+        self.bwd_group = bwd_group if bwd_group is not None else group
         A_pack, B_pack, table = model.packed()
         d_in = model.base.in_features
         self.k0, self.k1 = shard_columns(d_in, rank, world)
@@ -186,12 +190,12 @@ class ShardedLayer:
         t0, t1 = _share(b["n_tiles"], self.rank, self.world)
         c.bwd_dz(b, t0, t1)
         if b["dz"] is not None and self.world > 1:
-            dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.group)
+            dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.bwd_group)
         c.bwd_dx_da(b)
         b0, b1 = _share(b["n_db"], self.rank, self.world)
         c.bwd_db(b, b0, b1)
         if self.world > 1:
-            dist.all_reduce(b["dB"], op=dist.ReduceOp.SUM, group=self.group)
+            dist.all_reduce(b["dB"], op=dist.ReduceOp.SUM, group=self.bwd_group)
         return b["dx"], b["dA"], b["dB"]
 
     def step(self, x_p, plan, dy, n_nano: int, lr: float, pipelined: bool = True, comm: bool = True):
@@ -370,7 +374,8 @@ def _ksharded(args, rank, world, dev, comm_sms):
 
     sp = workloads.spec(args.workload, rows_scale=getattr(args, "rows_scale", 1.0))
     w = workloads.build(sp, device=dev)
-    layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms))
+    bwd_group = dist.new_group(list(range(world)))
+    layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms), bwd_group=bwd_group)
     x_p = layer.shard_input(w.x)
     plan = ops.route(w.ids.cpu(), layer.table, dev)
     lr = sp.lr

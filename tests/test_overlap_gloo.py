@@ -116,7 +116,7 @@ def _worker(rank, world, port, n_nano, pipelined, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         m, ids, x, dy = _build()
-        layer = ShardedLayer(m, rank, world, compute=DenseCompute())
+        layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group([0, 1]))
         plan = ops.route(ids, layer.table, torch.device("cpu"))
         x_p = layer.shard_input(x)
         y, dx_p = layer.step(x_p, plan, dy, n_nano, lr=0.01, pipelined=pipelined)
