@@ -170,6 +170,59 @@ def train_step(m, x, ids, dy, lr, plan=None):
     return y
 
 
+def ops_sizes(m, w, sp):
+    """Bytes of the low-rank intermediate Zt of this workload's routing plan."""
+    from tlora_b200 import ops
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(w.ids.cpu(), table, A_pack.device)
+    sc = np.array([float(a.scaling) for a in m.adapters.values()], dtype=np.float32)
+    return ops._CallArgs(sp.rows, sp.d_in, sp.d_out, ops.mlora_dtype(sp.dtype), "auto", plan, table, sc).sizes()[0]
+
+
+def rooflines(sp, kinds, zbytes, peaks_d, peaks_kind):
+    """Per kernel role: algorithmic work per launch / measured average launch
+    time against the bound that applies (tensor: the measured sustained bf16
+    GEMM peak, the kernels run inside a long step; HBM: the measured copy
+    bandwidth).  `traffic` = DRAM bytes per launch from the committed ncu
+    captures (profiles/traffic.json) where one exists for this workload."""
+    M, di, do = sp.rows, sp.d_in, sp.d_out
+    rsum = float(sum(r * n for r, n in zip(sp.ranks, sp.counts)))
+    e = 2  # bf16
+    rpack = sum(-(-r // 64) * 64 for r in sp.ranks)
+    work = {
+        "fwd_main": ("tensor", 2.0 * di * do * M + 2.0 * do * rsum),
+        "dx_main": ("tensor", 2.0 * di * do * M + 2.0 * di * rsum),
+        "fwd_shrink": ("hbm", e * M * di + zbytes + e * rpack * di),
+        "bwd_shrink": ("hbm", e * M * do + zbytes + e * rpack * do),
+        "dadb_reduce": ("hbm", e * M * (di + do) + 2 * zbytes + e * rpack * (di + do)),
+    }
+    traffic = {}
+    try:
+        t = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        if sp.name in t and abs(t[sp.name]["scaled_to_rows"] - M) < 1:
+            traffic = t[sp.name]["bytes_per_launch"]
+    except Exception:
+        pass
+    out = {}
+    for k, (ms_tot, n) in kinds.items():
+        if k not in work:
+            continue
+        bound, w = work[k]
+        avg = ms_tot / n
+        if bound == "tensor":
+            ach = w / (avg / 1000.0) / 1e12
+            peak = float(peaks_d.get("bf16_tflops_sustained", peaks_d.get("bf16_tflops")))
+            unit, pk = "TFLOP/s", f"{peaks_kind} sustained bf16 GEMM"
+        else:
+            ach = w / (avg / 1000.0) / 1e9
+            peak = float(peaks_d.get("hbm_gbs"))
+            unit, pk = "GB/s", f"{peaks_kind} HBM copy"
+        out[k] = {"bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": unit,
+                  "frac": round(ach / peak, 4), "peak_kind": pk, "algorithmic": w,
+                  "traffic": traffic.get(k), "avg_launch_ms": round(avg, 4)}
+    return out
+
+
 def cublas_backbone(w, dev, reps=10):
     """Context only: cuBLAS (torch.matmul) on the backbone GEMM shapes of the
     step, Y = X W^T and dX = dY W, without the LoRA terms."""
@@ -289,24 +342,11 @@ def run_single(args, peaks_d, peaks_kind):
 
     rows = sp.rows
     tokens_s = rows / (ms / 1000.0)
-    # roofline: the dominant tensor-core kernel is the fused forward mainloop
-    # (backbone + LoRA expand); its algorithmic FLOPs per launch are
-    # 2 d_in d_out M + 2 d_out sum_s n_s r_s
-    rsum = float(sum(r * n for r, n in zip(sp.ranks, sp.counts)))
     kinds = {k: v for k, v in ktimes.items() if v[1] > 0}
-    top = max(kinds, key=lambda k: kinds[k][0]) if kinds else "fwd_main"
-    flops_per_launch = {
-        "fwd_main": 2.0 * sp.d_in * sp.d_out * rows + 2.0 * sp.d_out * rsum,
-        "dx_main": 2.0 * sp.d_in * sp.d_out * rows + 2.0 * sp.d_in * rsum,
-    }
-    roof = None
-    if top in flops_per_launch and kinds:
-        avg_ms = kinds[top][0] / kinds[top][1]
-        achieved = flops_per_launch[top] / (avg_ms / 1000.0) / 1e12
-        peak = float(peaks_d.get("bf16_tflops_sustained", peaks_d.get("bf16_tflops")))
-        roof = {"bound": "tensor", "kernel": top, "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "peak_kind": f"{peaks_kind} sustained bf16",
-                "traffic": None, "avg_launch_ms": round(avg_ms, 4)}
+    zbytes = ops_sizes(m, w, sp)
+    roofs = rooflines(sp, kinds, zbytes, peaks_d, peaks_kind)
+    top = max(kinds, key=lambda k: kinds[k][0]) if kinds else None
+    roof = dict(roofs[top]) if top in roofs else None
     step_flops = sp.flops()
     out = {
         "metric": METRIC, "value": round(tokens_s, 1), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
@@ -320,6 +360,7 @@ def run_single(args, peaks_d, peaks_kind):
         "step_frac_of_peak": round(step_flops / (ms / 1000.0) / 1e12 /
                                    float(peaks_d.get("bf16_tflops_sustained", 1370.6)), 4),
         "roofline": roof,
+        "rooflines": roofs,
         "kernels_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in kinds.items()},
         "e2e": {"value": round(rows / (e2e_ms / 1000.0), 1), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": int(w.x.numel() * w.x.element_size()),
