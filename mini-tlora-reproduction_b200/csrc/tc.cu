@@ -57,13 +57,17 @@ constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kHalfRows = 128;       // rows of one CTA's A tile = TMEM lanes
-// 1-SM kernel: A 128x64 (16 KB) + B up to 256x64 (32 KB) per stage
-constexpr int kStages1 = 4;
+// 1-SM kernel: a 192 KB ring of stages, each A 128x64 (16 KB) + B up to
+// 256x64 (32 KB).  The mainloops use 4 stages of 48 KB; the HBM-bound roles,
+// whose B is narrower, cut the same ring into up to 8 smaller stages so that
+// more bytes are in flight per SM.
+constexpr int kMaxStages1 = 8;
 constexpr int kA1Bytes = 128 * 64 * 2;
 constexpr int kStage1Bytes = kA1Bytes + 256 * 64 * 2;
+constexpr int kRing1Bytes = 4 * kStage1Bytes;
 // epilogue staging: per epilogue warp two 32x32 bf16 buffers (64-byte swizzle)
 constexpr int kStageOutBytes = 4 * 2 * 32 * 32 * 2;  // 16 KB
-constexpr int kSmem1 = kStages1 * kStage1Bytes + kStageOutBytes + 1024 + 256;
+constexpr int kSmem1 = kRing1Bytes + kStageOutBytes + 1024 + 256;
 // 2-SM kernel: per CTA A 128x64 (16 KB) + B half 128x64 (16 KB) per stage
 constexpr int kStages2 = 6;
 constexpr int kA2Bytes = 128 * 64 * 2;
@@ -87,6 +91,8 @@ struct TcParams {
   int raster_n;     // main: 0 = groups of M tiles sweep all N blocks, 1 = groups of N blocks sweep all M
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
+  int n_stages;     // 1-SM kernel: stages of the ring (<= kMaxStages1)
+  int stage_bytes;  // 1-SM kernel: bytes per stage (multiple of 8 KB)
   int da_on;        // reduce: compute dA items
   int db0, db1;     // reduce: dB items of d_out blocks [db0, db1)
   const __nv_bfloat16* bias;
@@ -422,10 +428,11 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_out = smem + kStages1 * kStage1Bytes;
+  uint8_t* stage_out = smem + kRing1Bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
-  uint64_t* empty = full + kStages1;
-  uint64_t* tfull = empty + kStages1;  // [2]
+  uint64_t* empty = full + kMaxStages1;
+  uint64_t* tfull = empty + kMaxStages1;  // [2]
+  const int n_stages = p.n_stages, stage_bytes = p.stage_bytes;
   uint64_t* tempty = tfull + 2;        // [2]
   uint64_t* drain = tempty + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -437,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   constexpr int kUnits = 2;  // main modes run on 128-row halves of the plan tiles
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages1; ++s) {
+    for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       const int row0 = it.t * kTileRows + it.half * kHalfRows;  // first X / dY row of the A tile
       for (int kb = 0; kb < it.nk; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-        uint8_t* sA = smem + stage * kStage1Bytes;
+        uint8_t* sA = smem + stage * stage_bytes;
         uint8_t* sB = sA + kA1Bytes;
         uint64_t* bar = &full[stage];
         if (MODE == FWD_MAIN) {
@@ -523,13 +530,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         }
         issued |= 1u << stage;
         issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages1) { stage = 0; phase ^= 1; }
+        if (++stage == n_stages) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok) {
       // let copies already in flight land before the CTA exits
       const unsigned long long t0 = now_ns();
-      for (int s = 0; s < kStages1; ++s) {
+      for (int s = 0; s < n_stages; ++s) {
         if (!((issued >> s) & 1u)) continue;
         while (!mbar_try(su32(&full[s]), (issued_par >> s) & 1u)) {
           if (now_ns() - t0 > kTimeoutNs) break;
@@ -556,14 +563,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       for (int kb = 0; kb < it.nk; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sA = su32(smem + stage * kStage1Bytes);
+        const uint32_t sA = su32(smem + stage * stage_bytes);
         const uint64_t ad = sdesc(sA, a_lbo, 1024);
         const uint64_t bd = sdesc(sA + kA1Bytes, b_lbo, 1024);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc_mma(d, ad + uint64_t(k * a_step), bd + uint64_t(k * b_step), idesc, (kb | k) != 0);
         tc_commit(&empty[stage]);
-        if (++stage == kStages1) { stage = 0; phase ^= 1; }
+        if (++stage == n_stages) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
       tc_commit(&tfull[acc]);
@@ -885,9 +892,19 @@ int cta_budget(int max_ctas) {
   return sms;
 }
 
+// Ring of a 1-SM launch whose B operand is at most `b_boxes` 64x64 boxes wide
+// per stage (main modes: 4).
+void set_ring(TcParams& prm, int b_boxes) {
+  prm.stage_bytes = kA1Bytes + b_boxes * kBox64;
+  prm.n_stages = std::min(kMaxStages1, kRing1Bytes / prm.stage_bytes);
+}
+
 template <int MODE>
 int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
   if (prm.n_items <= 0) return MLORA_OK;
+  if (prm.n_stages < 2 || prm.n_stages > kMaxStages1 || prm.stage_bytes % 1024 != 0 ||
+      prm.n_stages * prm.stage_bytes > kRing1Bytes)
+    return MLORA_ERR_INVALID_ARG;
   const int sms = cta_budget(max_ctas);
   if (sms <= 0) return MLORA_ERR_CUDA;
   MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1));
@@ -941,6 +958,13 @@ bool raster_override(const char* var, TcParams& prm) {
   return true;
 }
 
+// widest shrink item (in 64-column chunks) of a range of shrink items
+int max_nc(std::vector<ShrinkItem>::const_iterator lo, std::vector<ShrinkItem>::const_iterator hi) {
+  int nc = 1;
+  for (auto it = lo; it != hi; ++it) nc = std::max(nc, int(it->nc));
+  return nc;
+}
+
 TcParams base_params(const TcCall& a) {
   TcParams prm;
   memset(&prm, 0, sizeof(prm));
@@ -976,6 +1000,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     prm.item0 = int(lo - sh.begin());
     prm.n_items = 2 * int(hi - lo);  // two 128-row halves per shrink item
     prm.nk_main = (a.d_in + 63) / 64;
+    set_ring(prm, max_nc(lo, hi));
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
     int s = launch1<SHRINK_FWD>(prm, st, a.max_ctas);
     if (s != MLORA_OK) return s;
@@ -1003,6 +1028,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     return launch2<FWD_MAIN>(prm, st, a.max_ctas);
   }
   prm.n_items = 2 * prm.n_tiles_rng * prm.n_nblk;
+  set_ring(prm, 4);
   return launch1<FWD_MAIN>(prm, st, a.max_ctas);
 }
 
@@ -1020,6 +1046,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.item0 = int(lo - sh.begin());
     prm.n_items = 2 * int(hi - lo);
     prm.nk_main = (a.d_out + 63) / 64;
+    set_ring(prm, max_nc(lo, hi));
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
     if ((s = launch1<SHRINK_BWD>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
@@ -1042,6 +1069,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
       s = launch2<DX_MAIN>(prm, st, a.max_ctas);
     } else {
       prm.n_items = 2 * a.plan.n_tiles * prm.n_nblk;
+      set_ring(prm, 4);
       s = launch1<DX_MAIN>(prm, st, a.max_ctas);
     }
     if (s != MLORA_OK) return s;
@@ -1059,6 +1087,9 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.da_on = da ? 1 : 0;
     prm.db0 = db ? a.db0 : 0;
     prm.db1 = db ? a.db1 : 0;
+    int nc = 1;
+    for (const ReduceItem& r : a.host->reduce) nc = std::max(nc, int(r.nc));
+    set_ring(prm, nc);  // A: two 64x64 boxes = kA1Bytes
     if ((s = launch1<REDUCE>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
   return MLORA_OK;
