@@ -115,7 +115,7 @@ int mlora_forward(const mlora_problem* prob, const mlora_routing* route,
 #define MLORA_STAGE_NO_EXPAND 4  /* with MAIN: leave the LoRA expand out (zsave is not read) */
 
 /* mlora_forward restricted to plan tiles [tile_begin, tile_end) (rows
- * [128*tile_begin, min(128*tile_end, rows)) of X and Y; Y, X and zsave are
+ * [MLORA_TILE_ROWS*tile_begin, min(MLORA_TILE_ROWS*tile_end, rows)) of X and Y; Y, X and zsave are
  * the full-batch buffers) and to the given stages.  Used by the nano-batch
  * pipeline (phase6_two_gpu_overlap.py:247-280): each nano-batch is a tile
  * range, and a K-sharded rank other than the one that owns the LoRA expand
@@ -126,7 +126,7 @@ int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
                          void* Y, void* zsave, void* workspace, size_t workspace_bytes,
                          int32_t stages, int32_t tile_begin, int32_t tile_end, void* stream);
 
-/* Number of 128-row plan tiles of a problem (ceil(rows / 128)). */
+/* Number of plan tiles of a problem (ceil(rows / MLORA_TILE_ROWS)). */
 int32_t mlora_num_tiles(int64_t rows);
 
 /* Fused forward for callers that cannot allocate device memory (no

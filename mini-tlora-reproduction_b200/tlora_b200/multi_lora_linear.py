@@ -52,7 +52,10 @@ class LoRAAdapter(nn.Module):
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         ids = torch.zeros(x2.shape[0], dtype=torch.int64)
-        packed = _PackedAdapters({"0": self})
+        packed = self.__dict__.get("_packed")
+        if packed is None or not packed.owns({"0": self}):
+            packed = _PackedAdapters({"0": self})
+            self.__dict__["_packed"] = packed
         y = packed.apply(x2, ids, None, None, impl="auto")
         return y.reshape(*lead, self.out_features)
 

@@ -15,14 +15,14 @@ sum_p Z_p = Z.  Per step:
 
   1. shrink: Z_p over all tiles, then an async SUM all-reduce of Z (small:
      128 x 64 bf16 per tile x rank chunk);
-  2. for each of N nano-batches (N near-equal ranges of 128-row tiles):
+  2. for each of N nano-batches (N near-equal ranges of 256-row plan tiles):
      the fused mainloop over its tiles, then an async SUM all-reduce of its
      rows of Y; nano-batch i+1's mainloop overlaps nano-batch i's all-reduce;
   3. backward with the replicated dY: dX_p = dY W_p + dZ A_p and
      dA_p = dZ^T X_p are local; dB = dY^T Z uses the all-reduced Z (computed
      identically on every rank, no exchange); then the isolated SGD step.
 
-Nano-batch boundaries are rounded to 128-row tiles (the reference splits rows
+Nano-batch boundaries are rounded to 256-row plan tiles (the reference splits rows
 exactly); N still counts nano-batches.
 """
 
