@@ -40,6 +40,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4"])
+    p.add_argument("--ksharded-workload", default="c3", choices=["c2", "c3", "c4"],
+                   help="N > 1: workload of the K-sharded nano-batch pipeline (the multi-GPU configuration "
+                        "is c3, 8192 x 8192 with 32 jobs)")
     p.add_argument("--rows-scale", type=float, default=1.0,
                    help="scale the rows of every adapter (profiling captures of a smaller case)")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -56,7 +56,8 @@ struct PlanDev {
   const ShrinkItem* shrink;         // [n_shrink]
   const ReduceItem* reduce;         // [n_reduce]
   const int32_t* list;              // [n_list] base chunk ids, grouped by adapter
-  int32_t* counters;                // [4] dynamic work counters (zeroed per launch)
+  int32_t* counters;                // [16] work counters of the persistent kernels, one per role;
+                                    // zeroed by every plan upload (one per API call)
 };
 
 // Host-side plan built from the routing description.

@@ -67,12 +67,13 @@ constexpr int kStage1Bytes = kA1Bytes + 256 * 64 * 2;
 constexpr int kRing1Bytes = 4 * kStage1Bytes;
 // epilogue staging: per epilogue warp two 32x32 bf16 buffers (64-byte swizzle)
 constexpr int kStageOutBytes = 4 * 2 * 32 * 32 * 2;  // 16 KB
-constexpr int kSmem1 = kRing1Bytes + kStageOutBytes + 1024 + 256;
+constexpr int kSched = 4;  // depth of the work-item queue from the producer to the MMA and epilogue warps
+constexpr int kSmem1 = kRing1Bytes + kStageOutBytes + 1024 + 512;
 // 2-SM kernel: per CTA A 128x64 (16 KB) + B half 128x64 (16 KB) per stage
 constexpr int kStages2 = 6;
 constexpr int kA2Bytes = 128 * 64 * 2;
 constexpr int kStage2Bytes = kA2Bytes + 128 * 64 * 2;
-constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOutBytes + 1024 + 256;
+constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOutBytes + 1024 + 512;
 
 enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
 
@@ -91,6 +92,7 @@ struct TcParams {
   int raster_n;     // main: 0 = groups of M tiles sweep all N blocks, 1 = groups of N blocks sweep all M
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
+  int* counter;     // work-item counter of this launch (zero at launch)
   int n_stages;     // 1-SM kernel: stages of the ring (<= kMaxStages1)
   int stage_bytes;  // 1-SM kernel: bytes per stage (multiple of 8 KB)
   int da_on;        // reduce: compute dA items
@@ -138,6 +140,19 @@ __device__ __forceinline__ bool mbar_try(uint32_t b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with cluster-scope acquire: for barriers that another CTA of the
+// cluster arrives on after writing this CTA's shared memory
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait.  Returns false if the CTA is aborting or the wait timed out
 // (then the CTA is flagged to abort and the device error word is set).
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
@@ -155,6 +170,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
       }
     }
   }
+}
+// bounded wait with cluster-scope acquire (see mbar_try_cluster)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = su32(b);
+  if (mbar_try_cluster(a, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_cluster(a, parity)) return true;
+    if ((i & 63) == 63) {
+      if (*abort_flag) return false;
+      if (now_ns() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicOr(&g_err_word, kErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+// store to the shared memory of a CTA of the cluster (shared::cluster address)
+__device__ __forceinline__ void st_cluster_s32(uint32_t addr, int32_t v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
@@ -364,6 +400,51 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
   return it;
 }
 
+// ------------------------------------------------------------------ tile scheduler
+// Work items are handed out dynamically: the producer thread of a CTA (of
+// the even CTA of a pair) takes the next item index from the launch's global
+// counter and publishes it in a ring of kSched shared-memory slots; the MMA
+// thread and every epilogue warp (and, in a pair, the odd CTA's producer and
+// epilogue warps) take the items from the ring in the same order.  A CTA that
+// starts late (its SM busy with another kernel, e.g. a collective running
+// beside the mainloop) simply takes fewer items, and items of unequal length
+// (ragged segments, reduce items sorted longest first) balance across CTAs.
+// Item -1 ends the queue.
+struct SchedQ {
+  volatile int32_t* item;  // [kSched]
+  uint64_t* full;          // [kSched], one arrival (the publishing producer)
+  uint64_t* empty;         // [kSched], one arrival per consumer
+  int q;
+  uint32_t ph;
+  __device__ __forceinline__ void advance() {
+    if (++q == kSched) { q = 0; ph ^= 1; }
+  }
+};
+// The producer claims its next item kClaimAhead k-blocks before the end of
+// the current one, so the atomic's round trip overlaps the last loads.
+constexpr int kClaimAhead = 8;
+// producer: publish the claimed item (claiming now if none is claimed yet,
+// claimed == -2) in this CTA's ring
+__device__ __forceinline__ bool sched_next(SchedQ& s, int* counter, int n_items, volatile int* abort_flag,
+                                           int& claimed, int& item) {
+  if (!mbar_wait(&s.empty[s.q], s.ph ^ 1, abort_flag)) return false;
+  const int i = claimed == -2 ? atomicAdd(counter, 1) : claimed;
+  claimed = -2;
+  item = i < n_items ? i : -1;
+  s.item[s.q] = item;
+  mbar_arrive(&s.full[s.q]);
+  s.advance();
+  return true;
+}
+// consumer: wait for the next published item (cluster-scope acquire when the
+// item was published by the other CTA of a pair)
+__device__ __forceinline__ bool sched_take(SchedQ& s, bool remote, volatile int* abort_flag, int& item) {
+  if (!(remote ? mbar_wait_cluster(&s.full[s.q], s.ph, abort_flag) : mbar_wait(&s.full[s.q], s.ph, abort_flag)))
+    return false;
+  item = s.item[s.q];
+  return true;
+}
+
 // ------------------------------------------------------------------ epilogues
 // Store one 32-column slice of the main accumulator (row `row` of Y / dX).
 // One 32-column slice of the main accumulator for the 32 rows of this warp
@@ -432,11 +513,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
   uint64_t* empty = full + kMaxStages1;
   uint64_t* tfull = empty + kMaxStages1;  // [2]
-  const int n_stages = p.n_stages, stage_bytes = p.stage_bytes;
   uint64_t* tempty = tfull + 2;        // [2]
   uint64_t* drain = tempty + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* sched_full = reinterpret_cast<uint64_t*>(const_cast<int*>(abort_flag) + 1);  // [kSched]
+  uint64_t* sched_empty = sched_full + kSched;                                          // [kSched]
+  volatile int32_t* sched_item = reinterpret_cast<volatile int32_t*>(sched_empty + kSched);
+  const int n_stages = p.n_stages, stage_bytes = p.stage_bytes;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   constexpr bool A_MN = MODE == REDUCE;
@@ -453,6 +537,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       mbar_init(&tempty[a], 128);
     }
     mbar_init(drain, 1);
+    for (int q = 0; q < kSched; ++q) {
+      mbar_init(&sched_full[q], 1);
+      mbar_init(&sched_empty[q], 1 + 4);  // the MMA thread and the four epilogue warps
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -475,11 +563,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     bool ok = true;
     const uint64_t pol_keep = policy_evict_last(), pol_stream = policy_evict_first(),
                    pol_norm = policy_evict_normal();
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    int claimed = -2;
+    for (int item = 0; ok;) {
+      if (!sched_next(sq, p.counter, p.n_items, abort_flag, claimed, item)) { ok = false; break; }
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
       const int row0 = it.t * kTileRows + it.half * kHalfRows;  // first X / dY row of the A tile
+      const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
       for (int kb = 0; kb < it.nk; ++kb) {
+        if (kb == claim_kb) claimed = atomicAdd(p.counter, 1);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
         uint8_t* sA = smem + stage * stage_bytes;
         uint8_t* sB = sA + kA1Bytes;
@@ -553,7 +647,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     const uint32_t a_lbo = A_MN ? uint32_t(kBox64) : 16u, b_lbo = B_MN ? uint32_t(kBox64) : 16u;
     const uint32_t a_step = A_MN ? (16 * 128) >> 4 : 32 >> 4;  // descriptor units per UMMA_K = 16
     const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    for (int item = 0; ok;) {
+      if (!sched_take(sq, false, abort_flag, item)) { ok = false; break; }
+      mbar_arrive(&sq.empty[sq.q]);
+      sq.advance();
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
@@ -591,7 +690,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     uint32_t slices = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    for (int item = 0;;) {
+      if (!sched_take(sq, false, abort_flag, item)) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sq.empty[sq.q]);
+      sq.advance();
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
@@ -687,11 +792,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
   uint64_t* drain = tempty + 2;        // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* sched_full = reinterpret_cast<uint64_t*>(const_cast<int*>(abort_flag) + 1);  // [kSched]
+  uint64_t* sched_empty = sched_full + kSched;  // [kSched] (used in the even CTA)
+  volatile int32_t* sched_item = reinterpret_cast<volatile int32_t*>(sched_empty + kSched);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t crank = cluster_rank();
   const bool leader = crank == 0;
-  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   constexpr bool B_MN = MODE == DX_MAIN;
 
   if (threadIdx.x == 0) {
@@ -704,6 +811,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       mbar_init(&tempty[a], 256);  // both CTAs' epilogue threads
     }
     mbar_init(drain, 1);
+    for (int q = 0; q < kSched; ++q) {
+      mbar_init(&sched_full[q], 1);
+      // even CTA: its MMA thread and epilogue warps, the odd CTA's producer and epilogue warps
+      mbar_init(&sched_empty[q], 2 * (1 + 4));
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -725,11 +837,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
     bool ok = true;
     const uint64_t pol_keep = policy_evict_last(), pol_norm = policy_evict_normal();
-    for (int item = pair; item < p.n_items && ok; item += n_pairs) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    const uint32_t peer_item0 = mapa(su32(const_cast<int32_t*>(sched_item)), 1);
+    const uint32_t peer_full0 = mapa(su32(sched_full), 1), even_empty0 = mapa(su32(sched_empty), 0);
+    int claimed = -2;
+    for (int item = 0; ok;) {
+      if (leader) {
+        // publish the claimed item (claim one now if none) to both CTAs
+        if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag)) { ok = false; break; }
+        const int i = claimed == -2 ? atomicAdd(p.counter, 1) : claimed;
+        claimed = -2;
+        item = i < p.n_items ? i : -1;
+        sq.item[sq.q] = item;
+        st_cluster_s32(peer_item0 + 4u * uint32_t(sq.q), item);
+        mbar_arrive(&sq.full[sq.q]);
+        mbar_arrive_cluster(peer_full0 + 8u * uint32_t(sq.q));
+      } else {
+        if (!sched_take(sq, true, abort_flag, item)) { ok = false; break; }
+        mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      }
+      sq.advance();
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
       const int row0 = it.t * kTileRows + int(crank) * kHalfRows;  // this CTA's A rows
       const int nh = it.nb * 256 + int(crank) * 128;               // this CTA's half of the N block
+      const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
       for (int kb = 0; kb < it.nk; ++kb) {
+        if (leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
         uint8_t* sA = smem + stage * kStage2Bytes;
         uint8_t* sB = sA + kA2Bytes;
@@ -777,7 +911,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     const uint32_t a_step = 32 >> 4;
     const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
     const uint32_t idesc = idesc_bf16(256, 256, false, B_MN);
-    for (int item = pair; item < p.n_items && ok; item += n_pairs) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    for (int item = 0; ok;) {
+      if (!sched_take(sq, false, abort_flag, item)) { ok = false; break; }
+      mbar_arrive(&sq.empty[sq.q]);
+      sq.advance();
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
@@ -812,7 +951,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     uint32_t slices = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int item = pair; item < p.n_items; item += n_pairs) {
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    const uint32_t even_empty0 = mapa(su32(sched_empty), 0);
+    for (int item = 0;;) {
+      if (!sched_take(sq, !leader, abort_flag, item)) break;
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&sq.empty[sq.q]);
+        else mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      }
+      sq.advance();
+      if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
@@ -908,6 +1057,7 @@ int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
   const int sms = cta_budget(max_ctas);
   if (sms <= 0) return MLORA_ERR_CUDA;
   MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1));
+  prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
   const int grid = prm.n_items < sms ? prm.n_items : sms;
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);
@@ -923,6 +1073,7 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
   const int sms = cta_budget(max_ctas);
   if (sms < 2) return MLORA_ERR_UNSUPPORTED;
   MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc2<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
+  prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
   const int pairs = std::min(prm.n_items, sms / 2);
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);

@@ -14,13 +14,16 @@ only), Z_p = s X_p A_p^T; since both are linear in X_p, sum_p Y_p = Y and
 sum_p Z_p = Z.  Per step:
 
   1. shrink: Z_p over all tiles, then an async SUM all-reduce of Z (small:
-     128 x 64 bf16 per tile x rank chunk);
+     256 x 64 bf16 per tile x rank chunk);
   2. for each of N nano-batches (N near-equal ranges of 256-row plan tiles):
      the fused mainloop over its tiles, then an async SUM all-reduce of its
      rows of Y; nano-batch i+1's mainloop overlaps nano-batch i's all-reduce;
-  3. backward with the replicated dY: dX_p = dY W_p + dZ A_p and
-     dA_p = dZ^T X_p are local; dB = dY^T Z uses the all-reduced Z (computed
-     identically on every rank, no exchange); then the isolated SGD step.
+  3. backward with the replicated dY, overlapping the Y all-reduces still in
+     flight: dZ = s dY B is split by tiles and dB = dY^T Z by 128-row blocks
+     of d_out across the ranks, each summed with a small all-reduce on a
+     second communicator (so it does not queue behind the Y traffic);
+     dX_p = dY W_p + dZ A_p and dA_p = dZ^T X_p are local; then the isolated
+     SGD step.
 
 Nano-batch boundaries are rounded to 256-row plan tiles (the reference splits rows
 exactly); N still counts nano-batches.
@@ -372,7 +375,7 @@ def _ksharded(args, rank, world, dev, comm_sms):
     steps and the prefetched e2e loop.  Returns the summary (rank 0)."""
     from . import _lib, workloads
 
-    sp = workloads.spec(args.workload, rows_scale=getattr(args, "rows_scale", 1.0))
+    sp = workloads.spec(getattr(args, "ksharded_workload", "c3"), rows_scale=getattr(args, "rows_scale", 1.0))
     w = workloads.build(sp, device=dev)
     bwd_group = dist.new_group(list(range(world)))
     layer = ShardedLayer(w.model, rank, world, compute=NativeCompute(comm_sms=comm_sms), bwd_group=bwd_group)
@@ -388,6 +391,12 @@ def _ksharded(args, rank, world, dev, comm_sms):
     for _ in range(max(3, args.warmup)):
         stepper(4)()
     torch.cuda.synchronize(dev)
+
+    # fixed nano-batch counts (the multi-GPU configuration's sweep N = 1, 2, 4, 8, 16)
+    n_sweep = {}
+    for n in (1, 2, 4, 8, 16):
+        if n <= n_tiles:
+            n_sweep[n] = _timed(stepper(n), 3, dev)
 
     # AIMD over the real pipelined step (phase6b_real_aimd.py:245-302)
     ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
@@ -424,4 +433,5 @@ def _ksharded(args, rank, world, dev, comm_sms):
                         "pipelined_ms": round(t_pipe, 4), "serial_ms": round(t_serial, 4),
                         "compute_only_ms": round(t_compute, 4), "comm_only_ms": round(t_comm, 4),
                         "comm_hidden_frac": round(hidden, 4)},
+            "n_sweep_ms": {str(k): round(v, 4) for k, v in n_sweep.items()},
             "aimd": horizons}
