@@ -64,10 +64,12 @@ def _share(total: int, rank: int, world: int) -> Tuple[int, int]:
 
 class NativeCompute:
     """The native kernels (tcgen05 for bf16) behind the sharded layer.
-    ``comm_sms`` SMs are left out of the nano-batch mainloops so the NCCL
-    all-reduce of the previous nano-batch has SMs to run on."""
+    ``comm_sms`` SMs can be left out of the mainloops that run beside the
+    NCCL all-reduces.  The kernels hand out work items dynamically, so CTAs
+    that find their SM taken by NCCL simply start later and take fewer items;
+    0 (no reservation) is the measured best on B200."""
 
-    def __init__(self, impl: str = "auto", comm_sms: int = 16):
+    def __init__(self, impl: str = "auto", comm_sms: int = 0):
         self.impl = impl
         self.comm_sms = int(comm_sms)
         self._sms = None
@@ -250,6 +252,12 @@ def _timed(fn, iters: int, device) -> float:
     return float(t.item())
 
 
+def _timed_med(fn, iters: int, device, reps: int = 3) -> float:
+    """Median of ``reps`` _timed measurements: the collectives' speed varies
+    from one measurement to the next on a shared node."""
+    return float(statistics.median(_timed(fn, iters, device) for _ in range(reps)))
+
+
 def _job_parallel(args, rank, world, dev, metric, unit):
     """Weak scaling without any collective on the data path: every rank trains
     its own set of jobs (same layer shape, its own adapters and rows, seeded
@@ -396,7 +404,7 @@ def _ksharded(args, rank, world, dev, comm_sms):
     n_sweep = {}
     for n in (1, 2, 4, 8, 16):
         if n <= n_tiles:
-            n_sweep[n] = _timed(stepper(n), 3, dev)
+            n_sweep[n] = _timed_med(stepper(n), 3, dev)
 
     # AIMD over the real pipelined step (phase6b_real_aimd.py:245-302)
     ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
@@ -411,17 +419,17 @@ def _ksharded(args, rank, world, dev, comm_sms):
     sm_sweep = {}
     for k in sorted({0, comm_sms // 2, comm_sms, comm_sms + comm_sms // 2}):
         layer.compute.comm_sms = k
-        sm_sweep[k] = _timed(stepper(best_n), 3, dev)
+        sm_sweep[k] = _timed_med(stepper(best_n), 3, dev)
     best_k = min(sm_sweep, key=sm_sweep.get)
     layer.compute.comm_sms = best_k
 
-    t_pipe = _timed(stepper(best_n), 3, dev)
-    t_serial = _timed(stepper(best_n, pipelined=False), 3, dev)
-    t_compute = _timed(stepper(best_n, comm=False), 3, dev)
+    t_pipe = _timed_med(stepper(best_n), 3, dev)
+    t_serial = _timed_med(stepper(best_n, pipelined=False), 3, dev)
+    t_compute = _timed_med(stepper(best_n, comm=False), 3, dev)
     y_buf, ctx = layer.forward(x_p, plan, best_n)
-    t_comm = _timed(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
+    t_comm = _timed_med(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
     hidden = 1.0 - max(0.0, t_pipe - t_compute) / t_comm if t_comm > 0 else 0.0
-    ms = _timed(stepper(best_n), args.steps, dev)
+    ms = _timed_med(stepper(best_n), args.steps, dev)
     del w
     if rank != 0:
         return None
