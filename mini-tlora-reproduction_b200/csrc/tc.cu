@@ -57,23 +57,27 @@ constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kHalfRows = 128;       // rows of one CTA's A tile = TMEM lanes
-// 1-SM kernel: a 192 KB ring of stages, each A 128x64 (16 KB) + B up to
-// 256x64 (32 KB).  The mainloops use 4 stages of 48 KB; the HBM-bound roles,
-// whose B is narrower, cut the same ring into up to 8 smaller stages so that
-// more bytes are in flight per SM.
-constexpr int kMaxStages1 = 8;
+// 1-SM kernel: a 216 KB ring of stages, each A 128x64 (16 KB) + B up to
+// 256x64 (32 KB), cut per launch: the mainloops use 4 stages of 48 KB, the
+// HBM-bound roles, whose B is narrower, up to 9 smaller stages, so that more
+// bytes are in flight per SM.  (32-column k-blocks with the 64-byte swizzle,
+// which would give the forward mainloop 9 stages of 24 KB, measured 45 %
+// slower than 4 stages of 64-column k-blocks.)
+constexpr int kMaxStages1 = 12;
 constexpr int kA1Bytes = 128 * 64 * 2;
-constexpr int kStage1Bytes = kA1Bytes + 256 * 64 * 2;
-constexpr int kRing1Bytes = 4 * kStage1Bytes;
-// epilogue staging: per epilogue warp two 32x32 bf16 buffers (64-byte swizzle)
-constexpr int kStageOutBytes = 4 * 2 * 32 * 32 * 2;  // 16 KB
+constexpr int kRing1Bytes = 216 * 1024;
+// epilogue staging (32x32 bf16 slices, 64-byte swizzle): one buffer per
+// epilogue warp in the 1-SM kernel, two in the 2-SM kernel
+constexpr int kStageOut1Bytes = 4 * 32 * 32 * 2;      // 8 KB
+constexpr int kStageOut2Bytes = 4 * 2 * 32 * 32 * 2;  // 16 KB
 constexpr int kSched = 4;  // depth of the work-item queue from the producer to the MMA and epilogue warps
-constexpr int kSmem1 = kRing1Bytes + kStageOutBytes + 1024 + 512;
+constexpr int kSmem1 = kRing1Bytes + kStageOut1Bytes + 1024 + 512;
 // 2-SM kernel: per CTA A 128x64 (16 KB) + B half 128x64 (16 KB) per stage
 constexpr int kStages2 = 6;
 constexpr int kA2Bytes = 128 * 64 * 2;
 constexpr int kStage2Bytes = kA2Bytes + 128 * 64 * 2;
-constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOutBytes + 1024 + 512;
+constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOut2Bytes + 1024 + 512;
+static_assert(kSmem1 <= 232448 && kSmem2 <= 232448, "dynamic shared memory above 227 KB");
 
 enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
 
@@ -247,6 +251,7 @@ __device__ __forceinline__ void tma_store(const CUtensorMap* map, uint32_t src, 
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -446,14 +451,14 @@ __device__ __forceinline__ bool sched_take(SchedQ& s, bool remote, volatile int*
 }
 
 // ------------------------------------------------------------------ epilogues
-// Store one 32-column slice of the main accumulator (row `row` of Y / dX).
 // One 32-column slice of the main accumulator for the 32 rows of this warp
 // (rows row_w0 .. row_w0 + 31 of Y / dX, lane = row): TMEM -> registers
 // (+ bias) -> bf16 in the warp's staging buffer -> one TMA store.  Warp-
 // collective: every lane calls it with the same arguments but its own TMEM
-// lane.  `buf` alternates between the warp's two buffers; the store issued
-// from the same buffer two slices earlier must have finished reading it.
-template <int MODE>
+// lane.  With NBUF = 2, `buf` alternates between the warp's two buffers; the
+// store issued from the same buffer NBUF slices earlier must have finished
+// reading it.
+template <int MODE, int NBUF>
 __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0, int n0, int col, bool empty_acc,
                                                uint32_t taddr, uint32_t buf, int lane) {
   const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
@@ -487,7 +492,10 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
         if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
     }
   }
-  if (lane == 0) bulk_wait_read_1();
+  if (lane == 0) {
+    if (NBUF == 2) bulk_wait_read_1();  // the store issued from this buffer two slices ago
+    else bulk_wait_read_0();            // the store issued from this buffer one slice ago
+  }
   __syncwarp();
   // row `lane` of the 32x32 box: 64 bytes, 16-byte chunk q at q ^ ((lane >> 1) & 3)
   const uint32_t rowb = buf + uint32_t(lane) * 64u;
@@ -510,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = smem + kRing1Bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOut1Bytes);
   uint64_t* empty = full + kMaxStages1;
   uint64_t* tfull = empty + kMaxStages1;  // [2]
   uint64_t* tempty = tfull + 2;        // [2]
@@ -579,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         uint8_t* sB = sA + kA1Bytes;
         uint64_t* bar = &full[stage];
         if (MODE == FWD_MAIN) {
-          mbar_expect_tx(bar, kStage1Bytes);
+          mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
           if (kb < it.nk1) {
             tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
             tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256, pol_keep);
@@ -589,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
             tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256, pol_keep);
           }
         } else if (MODE == DX_MAIN) {
-          mbar_expect_tx(bar, kStage1Bytes);
+          mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
           if (kb < it.nk1) {
             tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
             for (int i = 0; i < 4; ++i)
@@ -686,8 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
     const int r = quad * 32 + lane;  // accumulator row = TMEM lane
-    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 4096u;
-    uint32_t slices = 0;
+    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 2048u;
     int acc = 0;
     uint32_t acc_phase = 0;
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
@@ -710,8 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         const bool empty_acc = it.nk == 0;  // delta-only call on a tile without LoRA rows
         for (int col = 0; col < kAccCols; col += 32) {
           if (n0 + col >= N) break;
-          epi_main_slice<MODE>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
-          ++slices;
+          epi_main_slice<MODE, 1>(p, row_w0, n0, col, empty_acc, tbase + col, obuf, lane);
         }
       } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
         const int rt = it.half * kHalfRows + r;  // row inside the 256-row tile
@@ -785,7 +791,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = smem + kStages2 * kStage2Bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOutBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOut2Bytes);
   uint64_t* empty = full + kStages2;
   uint64_t* tfull = empty + kStages2;  // [2]
   uint64_t* tempty = tfull + 2;        // [2]  (used in the even CTA)
@@ -972,7 +978,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       const bool empty_acc = it.nk == 0;
       for (int col = 0; col < kAccCols; col += 32) {
         if (n0 + col >= N) break;
-        epi_main_slice<MODE>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
+        epi_main_slice<MODE, 2>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
         ++slices;
       }
       tc_fence_before();
@@ -1041,10 +1047,10 @@ int cta_budget(int max_ctas) {
   return sms;
 }
 
-// Ring of a 1-SM launch whose B operand is at most `b_boxes` 64x64 boxes wide
-// per stage (main modes: 4).
-void set_ring(TcParams& prm, int b_boxes) {
-  prm.stage_bytes = kA1Bytes + b_boxes * kBox64;
+// Ring of a 1-SM launch whose stages hold `a_bytes` of A and at most
+// `b_bytes` of B.
+void set_ring(TcParams& prm, int a_bytes, int b_bytes) {
+  prm.stage_bytes = a_bytes + b_bytes;
   prm.n_stages = std::min(kMaxStages1, kRing1Bytes / prm.stage_bytes);
 }
 
@@ -1151,7 +1157,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     prm.item0 = int(lo - sh.begin());
     prm.n_items = 2 * int(hi - lo);  // two 128-row halves per shrink item
     prm.nk_main = (a.d_in + 63) / 64;
-    set_ring(prm, max_nc(lo, hi));
+    set_ring(prm, kA1Bytes, max_nc(lo, hi) * kBox64);
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
     int s = launch1<SHRINK_FWD>(prm, st, a.max_ctas);
     if (s != MLORA_OK) return s;
@@ -1179,7 +1185,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     return launch2<FWD_MAIN>(prm, st, a.max_ctas);
   }
   prm.n_items = 2 * prm.n_tiles_rng * prm.n_nblk;
-  set_ring(prm, 4);
+  set_ring(prm, kA1Bytes, 4 * kBox64);
   return launch1<FWD_MAIN>(prm, st, a.max_ctas);
 }
 
@@ -1197,7 +1203,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.item0 = int(lo - sh.begin());
     prm.n_items = 2 * int(hi - lo);
     prm.nk_main = (a.d_out + 63) / 64;
-    set_ring(prm, max_nc(lo, hi));
+    set_ring(prm, kA1Bytes, max_nc(lo, hi) * kBox64);
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
     if ((s = launch1<SHRINK_BWD>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
@@ -1220,7 +1226,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
       s = launch2<DX_MAIN>(prm, st, a.max_ctas);
     } else {
       prm.n_items = 2 * a.plan.n_tiles * prm.n_nblk;
-      set_ring(prm, 4);
+      set_ring(prm, kA1Bytes, 4 * kBox64);
       s = launch1<DX_MAIN>(prm, st, a.max_ctas);
     }
     if (s != MLORA_OK) return s;
@@ -1240,7 +1246,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.db1 = db ? a.db1 : 0;
     int nc = 1;
     for (const ReduceItem& r : a.host->reduce) nc = std::max(nc, int(r.nc));
-    set_ring(prm, nc);  // A: two 64x64 boxes = kA1Bytes
+    set_ring(prm, kA1Bytes, nc * kBox64);  // A: two 64x64 boxes
     if ((s = launch1<REDUCE>(prm, st, a.max_ctas)) != MLORA_OK) return s;
   }
   return MLORA_OK;
