@@ -90,6 +90,13 @@ typedef struct mlora_routing {
   const int32_t* pack_off;    /* [n_adapters] first packed row/column, multiple of MLORA_RANK_CHUNK */
   const float* scaling;       /* [n_adapters] s_a = alpha_a / r_a */
   int32_t r_pack;             /* packed rank extent, multiple of MLORA_RANK_CHUNK */
+  const int32_t* out_rows;    /* optional DEVICE array [rows]: for callers whose rows were
+                                 sorted by adapter (mlora_route_sort's perm), the row of Y
+                                 (mlora_forward*) / of dX (mlora_backward*) that receives each
+                                 input row, so the output lands in the caller's original row
+                                 order without a scatter pass; NULL = identity.  Must be a
+                                 permutation of [0, rows) (tensor-core and CUDA-core paths).
+                                 Replaces the un-permute of tlora/multi_lora_linear.py:111-116. */
 } mlora_routing;
 
 /* Bytes of the forward->backward save buffer (the scaled, per-tile masked

@@ -119,7 +119,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
     a.host = &p;
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
     a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
-    a.Y = Y; a.zsave = zsave;
+    a.Y = Y; a.zsave = zsave; a.out_rows = route->out_rows;
     a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
     a.max_ctas = prob->max_ctas;
     a.pair_fwd = prob->impl == MLORA_IMPL_TC_2SM;
@@ -132,7 +132,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
   a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
   a.dtype = prob->dtype;
   a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
-  a.Y = Y; a.zsave = zsave;
+  a.Y = Y; a.zsave = zsave; a.out_rows = route->out_rows;
   a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
   a.c_begin = p.tile_chunk_begin[tile_begin];
   a.c_end = p.tile_chunk_begin[tile_end];
@@ -186,6 +186,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
     a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
     a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+    a.out_rows = route->out_rows;
     a.max_ctas = prob->max_ctas;
     a.pair_dx = prob->impl != MLORA_IMPL_TC_1SM;
     a.bwd_stages = stages; a.t0 = tile_begin; a.t1 = tile_end; a.db0 = db_begin; a.db1 = db_end;
@@ -199,6 +200,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
   a.dtype = prob->dtype;
   a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
   a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
+  a.out_rows = route->out_rows;
   a.bwd_stages = stages; a.db0 = db_begin; a.db1 = db_end;
   a.c_begin = p.tile_chunk_begin[tile_begin];
   a.c_end = p.tile_chunk_begin[tile_end];

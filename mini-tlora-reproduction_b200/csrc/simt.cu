@@ -100,8 +100,8 @@ template <class T, bool BWD>
 __global__ void __launch_bounds__(NT) k_main(PlanDev plan, const T* __restrict__ src,
                                               const T* __restrict__ W, const T* __restrict__ bias,
                                               const T* __restrict__ pack, const T* __restrict__ zt,
-                                              T* __restrict__ out, int64_t M, int d_in, int d_out,
-                                              int R, int t0, int no_expand) {
+                                              T* __restrict__ out, const int32_t* __restrict__ out_rows,
+                                              int64_t M, int d_in, int d_out, int R, int t0, int no_expand) {
   __shared__ float As[BK][LD], Bs[BK][LD];
   const int n0 = blockIdx.x * BN;
   const int64_t m0 = int64_t(t0) * kTileRows + int64_t(blockIdx.y) * BM;
@@ -149,13 +149,18 @@ __global__ void __launch_bounds__(NT) k_main(PlanDev plan, const T* __restrict__
   for (int i = 0; i < 4; ++i) {
     const int64_t row = m0 + ty * 4 + i;
     if (row >= M) continue;
+    const int64_t orow = out_rows ? int64_t(out_rows[row]) : row;  // caller's row order
+    if (orow < 0 || orow >= M) {  // out_rows is not a permutation of the rows
+      atomicOr(&g_err_word, kErrBounds);
+      continue;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= N) continue;
       float v = acc[i][j];
       if (!BWD && bias) v += to_f(bias[n]);
-      out[row * N + n] = from_f<T>(v);
+      out[orow * N + n] = from_f<T>(v);
     }
   }
 }
@@ -245,8 +250,8 @@ int launch_forward(const SimtCall& a, cudaStream_t st) {
     dim3 grid((a.d_out + BN - 1) / BN, unsigned((r1 - r0 + BM - 1) / BM));
     const int no_expand = (a.stages & MLORA_STAGE_NO_EXPAND) ? 1 : 0;
     k_main<T, false><<<grid, NT, 0, st>>>(a.plan, (const T*)a.X, (const T*)a.W, (const T*)a.bias,
-                                          (const T*)a.B_pack, (const T*)a.zsave, (T*)a.Y, a.M,
-                                          a.d_in, a.d_out, a.R, a.t0, no_expand);
+                                          (const T*)a.B_pack, (const T*)a.zsave, (T*)a.Y, a.out_rows,
+                                          a.M, a.d_in, a.d_out, a.R, a.t0, no_expand);
     count_launch();
   }
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -262,8 +267,8 @@ int launch_backward(const SimtCall& a, cudaStream_t st) {
   if (a.dX && (a.bwd_stages & MLORA_BWD_DX) && a.M > 0) {
     dim3 grid((a.d_in + BN - 1) / BN, unsigned((a.M + BM - 1) / BM));
     k_main<T, true><<<grid, NT, 0, st>>>(a.plan, (const T*)a.dY, (const T*)a.W, nullptr,
-                                         (const T*)a.A_pack, (const T*)a.dzt, (T*)a.dX, a.M,
-                                         a.d_in, a.d_out, a.R, 0, 0);
+                                         (const T*)a.A_pack, (const T*)a.dzt, (T*)a.dX, a.out_rows,
+                                         a.M, a.d_in, a.d_out, a.R, 0, 0);
     count_launch();
   }
   void* dA = (a.bwd_stages & MLORA_BWD_DA) ? a.dA : nullptr;

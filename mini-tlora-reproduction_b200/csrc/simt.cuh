@@ -17,6 +17,7 @@ struct SimtCall {
   void* zsave = nullptr;  // Zt (fwd output, bwd input)
   void* dzt = nullptr;    // dZt scratch (bwd)
   void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+  const int32_t* out_rows = nullptr;  // output row of each (sorted) input row of Y / dX, or identity
   // forward stages (MLORA_STAGE_*), plan tile range [t0, t1) and its chunk range
   int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
   int t0 = 0, t1 = 0, c_begin = 0, c_end = 0;

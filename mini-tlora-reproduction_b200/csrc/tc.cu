@@ -97,6 +97,7 @@ struct TcParams {
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
   int* counter;     // work-item counter of this launch (zero at launch)
+  const int32_t* out_rows;  // main modes: output row of each (sorted) input row, or nullptr
   int n_stages;     // 1-SM kernel: stages of the ring (<= kMaxStages1)
   int stage_bytes;  // 1-SM kernel: bytes per stage (multiple of 8 KB)
   int da_on;        // reduce: compute dA items
@@ -491,6 +492,24 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
       for (int q = 0; q < 32; ++q)
         if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
     }
+  }
+  if (p.out_rows) {
+    // rows sorted by adapter: each lane writes its row's 32 values straight to
+    // the row the caller's order puts it in (64 contiguous bytes)
+    const int64_t row = row_w0 + lane;
+    const int64_t orow = row < p.M ? int64_t(p.out_rows[row]) : -1;
+    if (row < p.M && (orow < 0 || orow >= p.M)) atomicOr(&g_err_word, kErrBounds);  // not a permutation
+    if (orow >= 0 && orow < p.M) {
+      __nv_bfloat16* dst = p.out + orow * N + n0 + col;
+      if (n0 + col + 32 <= N) {
+        store32_bf16(dst, f);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          if (n0 + col + q < N) dst[q] = __float2bfloat16_rn(f[q]);
+      }
+    }
+    return;
   }
   if (lane == 0) {
     if (NBUF == 2) bulk_wait_read_1();  // the store issued from this buffer two slices ago
@@ -1179,6 +1198,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
+  prm.out_rows = a.out_rows;
   if (!make_out_map(&prm.mY, a.Y, a.M, a.d_out)) return MLORA_ERR_UNSUPPORTED;
   if (a.pair_fwd) {
     prm.n_items = prm.n_tiles_rng * prm.n_nblk;
@@ -1220,6 +1240,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     if (!raster_override("MLORA_RASTER_DX", prm)) choose_raster(prm, a.pair_dx, prm.n_tiles_rng, prm.n_nblk, a.d_out);
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
+    prm.out_rows = a.out_rows;
     if (!make_out_map(&prm.mY, a.dX, a.M, a.d_in)) return MLORA_ERR_UNSUPPORTED;
     if (a.pair_dx) {
       prm.n_items = a.plan.n_tiles * prm.n_nblk;

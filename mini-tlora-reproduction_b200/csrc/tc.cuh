@@ -17,6 +17,7 @@ struct TcCall {
   void* zsave = nullptr;
   void* dzt = nullptr;
   void *dX = nullptr, *dA = nullptr, *dB = nullptr;
+  const int32_t* out_rows = nullptr;  // output row of each (sorted) input row of Y / dX, or identity
   // forward stages (MLORA_STAGE_*) and plan tile range [t0, t1)
   int stages = MLORA_STAGE_SHRINK | MLORA_STAGE_MAIN;
   int t0 = 0, t1 = 0;

@@ -71,6 +71,7 @@ class Routing(ctypes.Structure):
         ("pack_off", _c_int32_p),
         ("scaling", _c_float_p),
         ("r_pack", ctypes.c_int32),
+        ("out_rows", ctypes.c_void_p),  # device int32 [rows] or NULL
     ]
 
 

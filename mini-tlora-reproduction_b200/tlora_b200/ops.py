@@ -204,7 +204,7 @@ class _CallArgs:
     """Keeps the numpy arrays behind the ctypes structs alive for one call."""
 
     def __init__(self, rows, d_in, d_out, dtype, impl, plan: RoutePlan, table: AdapterTable,
-                 scaling: np.ndarray, max_ctas: int = 0):
+                 scaling: np.ndarray, max_ctas: int = 0, out_rows: Optional[torch.Tensor] = None):
         self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas))
         self.seg_start = np.ascontiguousarray(plan.seg_start, dtype=np.int32)
         self.seg_adapter = np.ascontiguousarray(plan.seg_adapter, dtype=np.int32)
@@ -214,7 +214,8 @@ class _CallArgs:
         self.route = _lib.Routing(
             len(self.seg_adapter), _lib.i32_ptr(self.seg_start), _lib.i32_ptr(self.seg_adapter),
             table.n, _lib.i32_ptr(self.rank), _lib.i32_ptr(self.pack_off), _lib.f32_ptr(self.scaling),
-            table.r_pack)
+            table.r_pack, out_rows.data_ptr() if out_rows is not None else None)
+        self.out_rows = out_rows  # kept alive for the call
 
     def sizes(self):
         z = ctypes.c_size_t(0)
@@ -239,11 +240,14 @@ class LayerState:
 
 def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     """Run mlora_forward; returns (Y in the caller's row order, zsave, x in
-    sorted order, call args)."""
+    sorted order, call args).  With interleaved ids the rows of X are
+    gathered into adapter order and the kernels write each row of Y straight
+    to its original position (mlora_routing.out_rows), with no scatter pass."""
     rows, d_in = x.shape
     d_out = st.B_pack.shape[0]
     xs = x_sorted if x_sorted is not None else (gather_rows(x, st.plan.perm) if st.plan.perm is not None else x)
-    args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling)
+    args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling,
+                     out_rows=st.plan.perm)
     zb, wb = args.sizes()
     dev = x.device
     y = torch.empty(rows, d_out, dtype=x.dtype, device=dev)
@@ -251,8 +255,6 @@ def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
     _lib.call("mlora_forward", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(xs), _ptr(W), _ptr(bias),
               _ptr(st.A_pack), _ptr(st.B_pack), _ptr(y), _ptr(z), _ptr(ws), wb, _stream(dev))
-    if st.plan.perm is not None:
-        y = scatter_rows(y, st.plan.perm)
     return y, z, xs, args
 
 
@@ -260,7 +262,7 @@ class StagedForward:
     """Forward of one routing plan split into stages and tile ranges (the
     nano-batch pipeline): ``shrink(t0, t1)`` writes the low-rank
     intermediate of tiles [t0, t1) into ``z``; ``main(t0, t1, expand)``
-    writes rows [128 t0, 128 t1) of ``y`` (backbone + bias, + LoRA expand when
+    writes rows [256 t0, 256 t1) of ``y`` (backbone + bias, + LoRA expand when
     ``expand``)."""
 
     def __init__(self, x, W, bias, st: LayerState, y=None):
@@ -300,13 +302,15 @@ class StagedForward:
 
 def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, want_dB: bool):
     """Run mlora_backward; returns (dX in the caller's row order or None,
-    dA_pack or None, dB_pack or None)."""
+    dA_pack or None, dB_pack or None).  dY is gathered into adapter order;
+    dX rows are written straight to their original positions."""
     rows = dy.shape[0]
     d_in = st.A_pack.shape[1]
     d_out = st.B_pack.shape[0]
     dev = dy.device
     dys = gather_rows(dy, st.plan.perm) if st.plan.perm is not None else dy
-    args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling)
+    args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
+                     out_rows=st.plan.perm)
     _, wb = args.sizes()
     ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
     dx = torch.empty(rows, d_in, dtype=dy.dtype, device=dev) if want_dx else None
@@ -317,8 +321,6 @@ def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, wan
     _lib.call("mlora_backward", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(dys), _ptr(xs), _ptr(W),
               _ptr(st.A_pack), _ptr(st.B_pack), _ptr(z), _ptr(dx), _ptr(dA), _ptr(dB), _ptr(ws), wb,
               _stream(dev))
-    if dx is not None and st.plan.perm is not None:
-        dx = scatter_rows(dx, st.plan.perm)
     return dx, dA, dB
 
 

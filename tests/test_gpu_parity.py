@@ -301,3 +301,60 @@ def test_scheduler_result_independent_of_cta_count(impl, max_ctas):
         o, r = int(table.pack_off[i]), int(table.rank[i])
         assert torch.equal(dA0[o:o + r], dA1[o:o + r])
         assert torch.equal(dB0[:, o:o + r], dB1[:, o:o + r])
+
+
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2")])
+def test_out_rows_writes_the_callers_row_order(dtype, impl):
+    """mlora_routing.out_rows: the forward writes row i of the (adapter-sorted)
+    input to row out_rows[i] of Y and the backward does the same for dX, bit
+    for bit what a separate scatter of the sorted outputs gives."""
+    import ctypes
+    from tlora_b200 import ops, _lib
+    m = _edge_module(256, 200, {0: 8, 1: 70, 2: 16}, dtype)
+    m.impl = impl
+    ids = torch.tensor([0] * 300 + [1] * 200 + [2] * 157, device=DEV)
+    rows = ids.shape[0]
+    x = torch.randn(rows, 256, device=DEV).to(dtype)
+    dy = torch.randn(rows, 200, device=DEV).to(dtype)
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(ids, table, torch.device(DEV))
+    scal = np.array([float(a.scaling) for a in m.adapters.values()], np.float32)
+    st = ops.LayerState(table, scal, plan, A_pack, B_pack, impl)
+    y_sorted, z, _, _ = ops.forward_raw(x, m.base.weight, m.base.bias, st)
+    dx_sorted, _, _ = ops.backward_raw(dy, x, m.base.weight, z, st, True, False, False)
+    perm = torch.randperm(rows, device=DEV).to(torch.int32)
+    st_p = ops.LayerState(table, scal, ops.RoutePlan(rows, plan.seg_start, plan.seg_adapter, perm, plan.active),
+                          A_pack, B_pack, impl)
+    y, z2, _, _ = ops.forward_raw(x, m.base.weight, m.base.bias, st_p, x_sorted=x)
+    dy_in = torch.empty_like(dy)
+    dy_in[perm.long()] = dy  # the backward gathers dY by perm back to the sorted rows
+    dx, _, _ = ops.backward_raw(dy_in, x, m.base.weight, z2, st_p, True, False, False)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    want_y = torch.empty_like(y_sorted)
+    want_y[perm.long()] = y_sorted
+    want_dx = torch.empty_like(dx_sorted)
+    want_dx[perm.long()] = dx_sorted
+    assert torch.equal(y, want_y)
+    assert torch.equal(dx, want_dx)
+
+
+def test_out_rows_outside_the_rows_sets_the_bounds_flag():
+    """An out_rows entry outside [0, rows) is not written: the kernel's own
+    bounds check skips the store and raises the device error word."""
+    from tlora_b200 import ops, _lib
+    m = _edge_module(256, 200, {0: 8}, torch.bfloat16)
+    ids = torch.zeros(300, dtype=torch.int64, device=DEV)
+    x = torch.randn(300, 256, device=DEV).to(torch.bfloat16)
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(ids, table, torch.device(DEV))
+    bad = torch.arange(300, dtype=torch.int32, device=DEV)
+    bad[7] = 300
+    st = ops.LayerState(table, np.array([1.5], np.float32),
+                        ops.RoutePlan(300, plan.seg_start, plan.seg_adapter, bad, plan.active), A_pack, B_pack, "tc")
+    _lib.clear_device_error()
+    y, _, _, _ = ops.forward_raw(x, m.base.weight, m.base.bias, st, x_sorted=x)
+    torch.cuda.synchronize()
+    assert _lib.device_error() & 1
+    _lib.clear_device_error()
+    assert _lib.device_error() == 0
