@@ -135,6 +135,37 @@ def multi_lora_backward(
     return dX, dA, dB
 
 
+def grad_projections(
+    x: np.ndarray,
+    ids: np.ndarray,
+    adapters: Dict[int, OracleAdapter],
+    dY: np.ndarray,
+    probes: Dict[int, Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]],
+) -> Dict[int, Tuple[np.ndarray, np.ndarray]]:
+    """Bilinear probes of the adapter gradients of ``multi_lora_backward``
+    without forming them, for checks at sizes where the full gradients are too
+    costly on a CPU: for adapter a and probe vectors (uA [k, r], vA [k, d_in],
+    uB [k, d_out], vB [k, r]) returns (uA_i^T dA vA_i, uB_i^T dB vB_i) for
+    i < k.  With the per-adapter formulas of phase5d_triton_training.py:287-312
+    (z = x A^T, dB = s g^T z, dz = s g B, dA = dz^T x):
+        u^T dA v = s (g (B u))^T (x v),   u^T dB v = s (g u)^T (x (A^T v)),
+    matrix-vector products only.  Adapters without rows are left out."""
+    _check_inputs(x, ids)
+    out: Dict[int, Tuple[np.ndarray, np.ndarray]] = {}
+    for aid, (uA, vA, uB, vB) in probes.items():
+        ad = adapters[aid]
+        mask = ids == aid
+        if not mask.any():
+            continue
+        xs = np.asarray(x[mask], dtype=np.float64)
+        g = np.asarray(dY[mask], dtype=np.float64)
+        # all k probes in one pass over g and x: column i is probe i
+        pa = ad.scaling * np.einsum("ni,ni->i", g @ (ad.B @ uA.T), xs @ vA.T)
+        pb = ad.scaling * np.einsum("ni,ni->i", g @ uB.T, xs @ (ad.A.T @ vB.T))
+        out[aid] = (pa, pb)
+    return out
+
+
 def sgd_step(param: np.ndarray, grad: Optional[np.ndarray], lr: float) -> np.ndarray:
     """Plain SGD, P <- P - lr * dP (phase5d_triton_training.py:554-559).
 

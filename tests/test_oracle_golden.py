@@ -107,3 +107,25 @@ def test_relative_l2():
     a = np.ones(4)
     assert orc.relative_l2(a, a) == 0.0
     assert abs(orc.relative_l2(2 * a, a) - 1.0) < 1e-12
+
+
+def test_grad_projections_match_full_gradients():
+    """The oracle's bilinear gradient probes equal u^T dA v and u^T dB v of the
+    full oracle gradients (used by the full-size GPU checks)."""
+    rng = np.random.default_rng(3)
+    d_in, d_out = 24, 20
+    ads = {a: orc.OracleAdapter(A=rng.standard_normal((r, d_in)), B=rng.standard_normal((d_out, r)), scaling=s)
+           for a, r, s in ((0, 3, 2.0), (4, 5, 0.5), (7, 2, 1.0))}
+    ids = rng.choice([0, 4, 9], size=50)
+    x = rng.standard_normal((50, d_in))
+    dy = rng.standard_normal((50, d_out))
+    W = rng.standard_normal((d_out, d_in))
+    _, dA, dB = orc.multi_lora_backward(x, ids, W, ads, dy)
+    probes = {a: (rng.standard_normal((4, ad.A.shape[0])), rng.standard_normal((4, d_in)),
+                  rng.standard_normal((4, d_out)), rng.standard_normal((4, ad.A.shape[0]))) for a, ad in ads.items()}
+    got = orc.grad_projections(x, ids, ads, dy, probes)
+    assert set(got) == {0, 4}  # adapter 7 owns no rows
+    for a, (pa, pb) in got.items():
+        uA, vA, uB, vB = probes[a]
+        np.testing.assert_allclose(pa, [u @ dA[a] @ v for u, v in zip(uA, vA)], rtol=1e-10, atol=1e-10)
+        np.testing.assert_allclose(pb, [u @ dB[a] @ v for u, v in zip(uB, vB)], rtol=1e-10, atol=1e-10)
