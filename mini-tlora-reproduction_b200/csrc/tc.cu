@@ -31,7 +31,12 @@
 //    of both CTAs.  Per SM this moves 2/3 of the operand bytes of a 1-SM
 //    128x256 tile for the same MMA work.
 //  * k_tc (SHRINK_*, REDUCE, and the 1-SM variant of the mainloops): one CTA,
-//    M = 128, N <= 256, 4 stages of 48 KB.
+//    M = 128, N <= 256, a 216 KB ring cut per launch (4 stages of 48 KB for a
+//    mainloop, up to 9 narrower stages for the HBM-bound roles).
+//
+// Work items are handed out dynamically (see "tile scheduler" below), and the
+// mainloop epilogues either TMA-store 32x32 slices or, when the rows were
+// sorted by adapter, store each row straight to the caller's row order.
 //
 // All operand tiles are 64 bf16 (128 B) wide with the 128-byte swizzle;
 // K-major operands are 128/256-row boxes, MN-major operands are stacks of
