@@ -55,6 +55,7 @@ extern "C" {
 /* element types */
 #define MLORA_F32 0
 #define MLORA_BF16 1
+#define MLORA_F16 2   /* fp16, the reference's GPU kernels' type (phase5c_fused_triton.py DTYPE) */
 
 /* adapter ranks are packed in chunks of this many rows/columns */
 #define MLORA_RANK_CHUNK 64
@@ -64,7 +65,7 @@ extern "C" {
 /* kernel family selection for mlora_forward / mlora_backward */
 #define MLORA_IMPL_AUTO 0   /* tcgen05 tensor-core kernels when the shape allows, else SIMT */
 #define MLORA_IMPL_SIMT 1   /* CUDA-core kernels, fp32 accumulate (exact fp32 mode) */
-#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 only); forward mainloop on single
+#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 or fp16); forward mainloop on single
                                SMs, dX mainloop on 2-SM pairs (the faster variant of each, measured) */
 #define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with both mainloops on single SMs (comparison path) */
 #define MLORA_IMPL_TC_2SM 4 /* as MLORA_IMPL_TC with both mainloops on 2-SM pairs (comparison path) */

@@ -49,7 +49,7 @@ int upload_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
 
 bool tc_shape_ok(const mlora_problem* prob) {
   // TMA: global strides must be multiples of 16 bytes (bf16: 8 elements)
-  return prob->dtype == MLORA_BF16 && prob->d_in % 8 == 0 && prob->d_out % 8 == 0;
+  return (prob->dtype == MLORA_BF16 || prob->dtype == MLORA_F16) && prob->d_in % 8 == 0 && prob->d_out % 8 == 0;
 }
 
 int choose_impl(const mlora_problem* prob) {
@@ -118,6 +118,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
     a.plan = dev;
     a.host = &p;
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+    a.dtype = prob->dtype;
     a.X = X; a.W = W; a.bias = bias; a.A_pack = A_pack; a.B_pack = B_pack;
     a.Y = Y; a.zsave = zsave; a.out_rows = route->out_rows;
     a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
@@ -184,6 +185,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
     a.plan = dev;
     a.host = &p;
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
+    a.dtype = prob->dtype;
     a.X = X; a.W = W; a.A_pack = A_pack; a.B_pack = B_pack; a.dY = dY;
     a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
     a.out_rows = route->out_rows;
@@ -230,7 +232,7 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
 extern "C" int mlora_sgd(const mlora_sgd_item* items, int32_t n_items, float lr, int32_t dtype,
                          void* stream) {
   if (n_items < 0 || (n_items > 0 && !items)) return MLORA_ERR_INVALID_ARG;
-  if (dtype != MLORA_F32 && dtype != MLORA_BF16) return MLORA_ERR_UNSUPPORTED;
+  if (dtype != MLORA_F32 && dtype != MLORA_BF16 && dtype != MLORA_F16) return MLORA_ERR_UNSUPPORTED;
   for (int i = 0; i < n_items; ++i) {
     const mlora_sgd_item& it = items[i];
     if (it.rows < 0 || it.cols < 0) return MLORA_ERR_INVALID_ARG;

@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include <atomic>
@@ -81,7 +82,7 @@ int build_plan(const mlora_problem* prob, const mlora_routing* route, Plan* plan
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // bytes of one element
-inline int elem_bytes(int dtype) { return dtype == MLORA_BF16 ? 2 : 4; }
+inline int elem_bytes(int dtype) { return dtype == MLORA_F32 ? 4 : 2; }
 
 // launch accounting
 extern std::atomic<int64_t> g_launches;
@@ -109,6 +110,8 @@ template <> __device__ __forceinline__ float from_f<float>(float v) { return v; 
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
 }  // namespace mlora
 

@@ -21,7 +21,7 @@ static int validate(const mlora_problem* prob, const mlora_routing* r) {
   if (!prob || !r) return MLORA_ERR_INVALID_ARG;
   if (prob->rows < 0 || prob->rows > (int64_t(1) << 31) - kTileRows) return MLORA_ERR_INVALID_ARG;
   if (prob->d_in < 1 || prob->d_out < 1) return MLORA_ERR_INVALID_ARG;
-  if (prob->dtype != MLORA_F32 && prob->dtype != MLORA_BF16) return MLORA_ERR_UNSUPPORTED;
+  if (prob->dtype != MLORA_F32 && prob->dtype != MLORA_BF16 && prob->dtype != MLORA_F16) return MLORA_ERR_UNSUPPORTED;
   if (prob->max_ctas < 0) return MLORA_ERR_INVALID_ARG;
   if (r->n_seg < 0 || r->n_adapters < 0) return MLORA_ERR_INVALID_ARG;
   if (r->r_pack < 0 || r->r_pack % kChunk) return MLORA_ERR_INVALID_ARG;

@@ -146,7 +146,8 @@ __global__ void k_rows(const V* __restrict__ src, const int32_t* __restrict__ pe
 
 int rows_copy(const void* src, const int32_t* perm, int64_t rows, int32_t cols, int32_t dtype,
               void* dst, cudaStream_t st, bool gather) {
-  if (rows < 0 || cols < 0 || (dtype != MLORA_F32 && dtype != MLORA_BF16)) return MLORA_ERR_INVALID_ARG;
+  if (rows < 0 || cols < 0 || (dtype != MLORA_F32 && dtype != MLORA_BF16 && dtype != MLORA_F16))
+    return MLORA_ERR_INVALID_ARG;
   if (rows == 0 || cols == 0) return MLORA_OK;
   if (!src || !perm || !dst) return MLORA_ERR_INVALID_ARG;
   const int64_t bytes = int64_t(cols) * elem_bytes(dtype);

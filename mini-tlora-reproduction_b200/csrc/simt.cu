@@ -304,17 +304,22 @@ int launch_sgd(const mlora_sgd_item* items, int n, float lr, cudaStream_t st) {
 }  // namespace
 
 int simt_forward(const SimtCall& a, cudaStream_t st) {
-  return a.dtype == MLORA_BF16 ? launch_forward<__nv_bfloat16>(a, st) : launch_forward<float>(a, st);
+  if (a.dtype == MLORA_BF16) return launch_forward<__nv_bfloat16>(a, st);
+  if (a.dtype == MLORA_F16) return launch_forward<__half>(a, st);
+  return launch_forward<float>(a, st);
 }
 
 int simt_backward(const SimtCall& a, cudaStream_t st) {
-  return a.dtype == MLORA_BF16 ? launch_backward<__nv_bfloat16>(a, st)
-                               : launch_backward<float>(a, st);
+  if (a.dtype == MLORA_BF16) return launch_backward<__nv_bfloat16>(a, st);
+  if (a.dtype == MLORA_F16) return launch_backward<__half>(a, st);
+  return launch_backward<float>(a, st);
 }
 
 int sgd_items(int dtype, const mlora_sgd_item* items, int n, float lr, cudaStream_t st) {
   if (n == 0) return MLORA_OK;
-  return dtype == MLORA_BF16 ? launch_sgd<__nv_bfloat16>(items, n, lr, st) : launch_sgd<float>(items, n, lr, st);
+  if (dtype == MLORA_BF16) return launch_sgd<__nv_bfloat16>(items, n, lr, st);
+  if (dtype == MLORA_F16) return launch_sgd<__half>(items, n, lr, st);
+  return launch_sgd<float>(items, n, lr, st);
 }
 
 }  // namespace mlora

@@ -107,7 +107,8 @@ struct TcParams {
   int stage_bytes;  // 1-SM kernel: bytes per stage (multiple of 8 KB)
   int da_on;        // reduce: compute dA items
   int db0, db1;     // reduce: dB items of d_out blocks [db0, db1)
-  const __nv_bfloat16* bias;
+  int f16;             // 16-bit elements are fp16 (else bf16)
+  const __nv_bfloat16* bias;  // 16-bit elements (bf16 or fp16, see f16)
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
   __nv_bfloat16* dA;
   __nv_bfloat16* dB;
@@ -319,22 +320,41 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) |
          (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
-// Instruction descriptor: bf16 x bf16 -> fp32, M = m, N = n.
-__device__ __forceinline__ uint32_t idesc_bf16(int m, int n, bool a_mn, bool b_mn) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+// Instruction descriptor of kind::f16: A and B both bf16 (or both fp16 when
+// f16) -> fp32 accumulator, M = m, N = n.
+__device__ __forceinline__ uint32_t idesc_16(int m, int n, bool a_mn, bool b_mn, bool f16) {
+  const uint32_t fmt = f16 ? 0u : 1u;  // 0 = F16, 1 = BF16 for both operands
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
          (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+// 16-bit element conversions (round to nearest even): fp16 when f16, else bf16
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
+  if (f16) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float (&f)[32]) {
+__device__ __forceinline__ float2 unpack2(uint32_t w, bool f16) {
+  if (f16) return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+__device__ __forceinline__ void st1(__nv_bfloat16* dst, float v, bool f16) {
+  *reinterpret_cast<uint16_t*>(dst) =
+      f16 ? __half_as_ushort(__float2half_rn(v)) : __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ float ld1(const __nv_bfloat16* src, bool f16) {
+  const unsigned short b = *reinterpret_cast<const unsigned short*>(src);
+  return f16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+}
+__device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&f)[32], bool f16) {
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    d4[q] = make_uint4(pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
-                       pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+    d4[q] = make_uint4(pack2(f[8 * q], f[8 * q + 1], f16), pack2(f[8 * q + 2], f[8 * q + 3], f16),
+                       pack2(f[8 * q + 4], f[8 * q + 5], f16), pack2(f[8 * q + 6], f[8 * q + 7], f16));
 }
 
 // ------------------------------------------------------------------ items
@@ -487,15 +507,15 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
-          f[8 * q + 2 * e] += __low2float(h);
-          f[8 * q + 2 * e + 1] += __high2float(h);
+          const float2 h = unpack2(w[e], p.f16);
+          f[8 * q + 2 * e] += h.x;
+          f[8 * q + 2 * e + 1] += h.y;
         }
       }
     } else {
 #pragma unroll
       for (int q = 0; q < 32; ++q)
-        if (n0 + col + q < N) f[q] += __bfloat162float(p.bias[n0 + col + q]);
+        if (n0 + col + q < N) f[q] += ld1(p.bias + n0 + col + q, p.f16);
     }
   }
   if (p.out_rows) {
@@ -507,11 +527,11 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
     if (orow >= 0 && orow < p.M) {
       __nv_bfloat16* dst = p.out + orow * N + n0 + col;
       if (n0 + col + 32 <= N) {
-        store32_bf16(dst, f);
+        store32(dst, f, p.f16);
       } else {
 #pragma unroll
         for (int q = 0; q < 32; ++q)
-          if (n0 + col + q < N) dst[q] = __float2bfloat16_rn(f[q]);
+          if (n0 + col + q < N) st1(dst + q, f[q], p.f16);
       }
     }
     return;
@@ -526,8 +546,9 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
   const uint32_t sw = uint32_t(lane >> 1) & 3u;
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    sts128(rowb + ((uint32_t(q) ^ sw) << 4), pack_bf16(f[8 * q], f[8 * q + 1]), pack_bf16(f[8 * q + 2], f[8 * q + 3]),
-           pack_bf16(f[8 * q + 4], f[8 * q + 5]), pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+    sts128(rowb + ((uint32_t(q) ^ sw) << 4), pack2(f[8 * q], f[8 * q + 1], p.f16),
+           pack2(f[8 * q + 2], f[8 * q + 3], p.f16), pack2(f[8 * q + 4], f[8 * q + 5], p.f16),
+           pack2(f[8 * q + 6], f[8 * q + 7], p.f16));
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
@@ -690,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(acc * kAccCols);
-      const uint32_t idesc = idesc_bf16(128, it.n, A_MN, B_MN);
+      const uint32_t idesc = idesc_16(128, it.n, A_MN, B_MN, p.f16 != 0);
       for (int kb = 0; kb < it.nk; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
         tc_fence_after();
@@ -754,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
             float f[32];
 #pragma unroll
             for (int q = 0; q < 32; ++q) f[q] = in ? ch.scale * __uint_as_float(v[q]) : 0.f;
-            store32_bf16(dst + col, f);
+            store32(dst + col, f, p.f16);
           }
         }
       } else {  // REDUCE
@@ -774,18 +795,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
                 float f[32];
 #pragma unroll
                 for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
-                store32_bf16(dst, f);
+                store32(dst, f, p.f16);
               } else {
 #pragma unroll
                 for (int q = 0; q < 32; ++q)
-                  if (col + q < rvalid) dst[q] = __float2bfloat16_rn(__uint_as_float(v[q]));
+                  if (col + q < rvalid) st1(dst + q, __uint_as_float(v[q]), p.f16);
               }
             } else {
               if (d >= p.d_in) continue;
 #pragma unroll
               for (int q = 0; q < 32; ++q)
                 if (col + q < rvalid)
-                  p.dA[int64_t(pcol + col + q) * p.d_in + d] = __float2bfloat16_rn(__uint_as_float(v[q]));
+                  st1(p.dA + int64_t(pcol + col + q) * p.d_in + d, __uint_as_float(v[q]), p.f16);
             }
           }
         }
@@ -940,7 +961,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     const uint32_t b_lbo = B_MN ? uint32_t(kBox64) : 16u;
     const uint32_t a_step = 32 >> 4;
     const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
-    const uint32_t idesc = idesc_bf16(256, 256, false, B_MN);
+    const uint32_t idesc = idesc_16(256, 256, false, B_MN, p.f16 != 0);
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     for (int item = 0; ok;) {
       if (!sched_take(sq, false, abort_flag, item)) { ok = false; break; }
@@ -1039,7 +1060,9 @@ EncodeFn get_encode() {
   return fn;
 }
 
-// 2-D bf16 map over a row-major [rows, cols] matrix; box = box_cols x box_rows
+// 2-D map over a row-major [rows, cols] matrix of 16-bit elements (bf16 or
+// fp16: the copies only move bytes, and out-of-bounds fill is zero bits, +0 in
+// both formats); box = box_cols x box_rows
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int box_cols = 64,
               CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeFn enc = get_encode();
@@ -1149,6 +1172,7 @@ int max_nc(std::vector<ShrinkItem>::const_iterator lo, std::vector<ShrinkItem>::
 TcParams base_params(const TcCall& a) {
   TcParams prm;
   memset(&prm, 0, sizeof(prm));
+  prm.f16 = a.dtype == MLORA_F16 ? 1 : 0;
   prm.plan = a.plan;
   prm.M = a.M;
   prm.d_in = a.d_in;

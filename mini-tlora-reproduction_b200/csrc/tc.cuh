@@ -11,6 +11,7 @@ struct TcCall {
   const Plan* host = nullptr;
   int64_t M = 0;
   int d_in = 0, d_out = 0, R = 0;
+  int dtype = MLORA_BF16;  // MLORA_BF16 or MLORA_F16
   const void *X = nullptr, *W = nullptr, *bias = nullptr, *A_pack = nullptr, *B_pack = nullptr;
   const void* dY = nullptr;
   void* Y = nullptr;

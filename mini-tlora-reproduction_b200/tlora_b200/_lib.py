@@ -27,6 +27,7 @@ ERR_TIMEOUT = 6
 
 F32 = 0
 BF16 = 1
+F16 = 2
 
 RANK_CHUNK = 64
 TILE_ROWS = 256

@@ -20,11 +20,11 @@ reduction "sum" against a per-job target, backward, per-job SGD (lr 1e-5).
 The baselines use torch.optim.SGD per adapter as the reference does; the
 fused mode uses MultiLoRALinear.sgd_step, which updates the same tensors.
 
-    python -m tlora_b200.compare [--workload phase5a|c2] [--warmup 10] [--iters 40]
+    python -m tlora_b200.compare [--workload phase5a|c2] [--dtype fp16|bf16] [--warmup 10] [--iters 40]
 
 The phase5a workload is the reference's (4096 -> 4096, jobs ranks 2/4/8/16
-with batches 32/64/16/128), in bf16 instead of fp16 (the tensor-core path
-computes bf16).  c2 is the 4096 -> 11008 training-step shape (8 jobs, ranks
+with batches 32/64/16/128) in its element type, fp16 (the default; bf16 on
+request).  c2 is the 4096 -> 11008 training-step shape (8 jobs, ranks
 alternating 16/64, 8192 rows each).  Inputs are seeded synthetic tensors.
 """
 
@@ -174,12 +174,12 @@ def _opts(params_by_job):
     return {aid: torch.optim.SGD(list(ps), lr=LR) for aid, ps in params_by_job.items()}
 
 
-def build_modes(jb: Jobs, device="cuda"):
+def build_modes(jb: Jobs, device="cuda", dtype=torch.bfloat16):
     """The four modes, each with its own copy of the same initial weights,
     as {name: (step_fn, adapters_fn)}; adapters_fn returns the mode's
     LoRAAdapter of each job (weights and gradients after a step)."""
-    seed = make_seed(jb, device)
-    xs, ys, x_all, y_all, spans, ids = make_data(jb, device)
+    seed = make_seed(jb, device, dtype)
+    xs, ys, x_all, y_all, spans, ids = make_data(jb, device, dtype)
     ind = make_independent(seed, jb)
     ind_opts = _opts({a: m.adapter.parameters() for a, m in ind.items()})
     naive = clone_shared(seed, jb)
@@ -209,7 +209,7 @@ def build_modes(jb: Jobs, device="cuda"):
 
 def forward_error(seed, xs, x_all, ids, spans):
     """phase5_gpu_baseline.py:331-365: the fused shared forward against the
-    per-job formula, computed in fp32 from the same bf16 weights."""
+    per-job formula, computed in fp32 from the same 16-bit weights."""
     with torch.no_grad():
         y = seed(x_all, ids).float()
         W = seed.base.weight.float()
@@ -250,15 +250,17 @@ def time_mode(fn, warmup: int, iters: int, rows: int) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--workload", default="phase5a", choices=["phase5a", "c2", "tiny"])
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--iters", type=int, default=40)
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("a CUDA device is required")
     jb = jobs(a.workload)
-    modes, pbytes, (seed, xs, x_all, spans, ids) = build_modes(jb)
+    dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
+    modes, pbytes, (seed, xs, x_all, spans, ids) = build_modes(jb, dtype=dt)
     err, rel = forward_error(seed, xs, x_all, ids, spans)
-    print(f"workload {jb.name}: {jb.d_in} -> {jb.d_out}, jobs {len(jb.rank)}, rows {jb.rows}, bf16")
+    print(f"workload {jb.name}: {jb.d_in} -> {jb.d_out}, jobs {len(jb.rank)}, rows {jb.rows}, {a.dtype}")
     print(f"fused shared forward vs per-job formula: max abs error {err:.3e}, relative L2 {rel:.3e}")
     red = 100.0 * (1.0 - pbytes["shared"] / pbytes["independent"])
     print(f"parameter storage: independent {pbytes['independent'] / 2**20:.2f} MB, "
@@ -269,7 +271,7 @@ def main(argv=None):
     print(f"{'mode':16s}{'mean ms':>10s}{'median ms':>11s}{'samples/s':>14s}{'peak MB':>10s}")
     for name, r in res.items():
         print(f"{name:16s}{r['mean_ms']:10.3f}{r['median_ms']:11.3f}{r['samples_s']:14.1f}{r['peak_mb']:10.1f}")
-    print(json.dumps({"workload": jb.name, "rows": jb.rows, "forward_max_abs_err": err, "forward_rel_l2": rel,
+    print(json.dumps({"workload": jb.name, "dtype": a.dtype, "rows": jb.rows, "forward_max_abs_err": err, "forward_rel_l2": rel,
                       "param_mb": {k: round(v / 2**20, 2) for k, v in pbytes.items()}, "modes": res}))
 
 

@@ -18,16 +18,16 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import BF16, F32, RANK_CHUNK, TILE_ROWS
+from ._lib import BF16, F16, F32, RANK_CHUNK, TILE_ROWS
 
-_DTYPES = {torch.float32: F32, torch.bfloat16: BF16}
+_DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 _IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC, "tc1": _lib.IMPL_TC_1SM,
           "tc2": _lib.IMPL_TC_2SM}
 
 
 def mlora_dtype(dt: torch.dtype) -> int:
     if dt not in _DTYPES:
-        raise NotImplementedError(f"dtype {dt} is not supported (float32 or bfloat16)")
+        raise NotImplementedError(f"dtype {dt} is not supported (float32, bfloat16 or float16)")
     return _DTYPES[dt]
 
 

@@ -152,6 +152,33 @@ def test_bf16_configs_scaled(cfg, scale, impl):
     assert_parity(got, want, BF16_TOL, f"{cfg} x{scale} {impl}")
 
 
+@pytest.mark.parametrize("cfg,scale", [("c2", 0.0625), ("c4", 0.03125)])
+@pytest.mark.parametrize("impl", ["tc", "tc2", "simt"])
+def test_fp16_configs_scaled(cfg, scale, impl):
+    """fp16, the element type of the reference's GPU kernels
+    (phase5c_fused_triton.py, phase5d_triton_training.py): forward, backward
+    and the isolated SGD step against the fp64 oracle on the same
+    fp16-rounded inputs, within the 16-bit tolerance."""
+    w = workloads.build(workloads.spec(cfg, scale), device=DEV, dtype=torch.float16)
+    m = w.model
+    m.impl = impl
+    got = module_step(m, w.x, w.ids, w.dy)
+    want = oracle_step(m, w.x, w.ids, w.dy)
+    assert_parity(got, want, BF16_TOL, f"{cfg} x{scale} fp16 {impl}")
+    before = {int(k): (to_np(a.A), to_np(a.B)) for k, a in m.adapters.items()}
+    m.sgd_step(0.05)
+    torch.cuda.synchronize()
+    for k, a in m.adapters.items():
+        k = int(k)
+        if want[2][k] is None:
+            assert np.array_equal(to_np(a.A), before[k][0])
+            continue
+        step_A = to_np(a.A) - before[k][0]
+        step_B = to_np(a.B) - before[k][1]
+        assert orc.relative_l2(step_A, -0.05 * want[2][k]) <= BF16_TOL
+        assert orc.relative_l2(step_B, -0.05 * want[3][k]) <= BF16_TOL
+
+
 def _edge_module(d_in, d_out, ranks, dtype, seed=0, bias_std=0.1):
     torch.manual_seed(seed)
     m = MultiLoRALinear(d_in, d_out, ranks)
@@ -178,7 +205,8 @@ EDGE_CASES = {
 }
 
 
-@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2")])
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2"),
+                                        (torch.float16, "tc1"), (torch.float16, "tc2"), (torch.float16, "simt")])
 @pytest.mark.parametrize("case", sorted(EDGE_CASES))
 def test_edge_cases(case, dtype, impl):
     d_in, d_out, ranks, idf = EDGE_CASES[case]
@@ -192,7 +220,8 @@ def test_edge_cases(case, dtype, impl):
     assert_parity(module_step(m, x, ids, dy), oracle_step(m, x, ids, dy), tol, case)
 
 
-@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2")])
+@pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2"),
+                                        (torch.float16, "tc")])
 def test_delta_only(dtype, impl):
     """add_base=False: only the LoRA delta (the reference kernel's ADD_BASE=False)."""
     m = _edge_module(256, 256, {0: 8, 1: 16, 2: 64}, dtype, bias_std=0.0)
