@@ -403,30 +403,57 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
   it.skip = false;
   it.nb = 0;
   it.half = 0;
+  // The plan tables are built and validated on the host; an index outside
+  // them here means a corrupted plan: every role flags it in the device error
+  // word and skips the item the same way, so no load or store goes out of
+  // the tables' bounds.
+  bool bad = false;
+  it.nc = 0;
+  it.nk1 = it.nk = 0;
+  it.n = 64;
+  it.c0 = 0;
+  it.t = 0;
   if (MODE == FWD_MAIN || MODE == DX_MAIN) {
     raster(p, item, units, it);
-    it.c0 = p.plan.tile_chunk_begin[it.t];
-    it.nc = p.no_expand ? 0 : p.plan.tile_chunk_begin[it.t + 1] - it.c0;
+    bad = it.t < 0 || it.t >= p.plan.n_tiles;
+    if (!bad) {
+      it.c0 = p.plan.tile_chunk_begin[it.t];
+      it.nc = p.no_expand ? 0 : p.plan.tile_chunk_begin[it.t + 1] - it.c0;
+      bad = it.c0 < 0 || it.nc < 0 || it.c0 + it.nc > p.plan.n_chunks;
+    }
     it.nk1 = p.nk_main;
     it.nk = it.nk1 + it.nc;
     it.n = kAccCols;
   } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
-    const ShrinkItem s = p.plan.shrink[p.item0 + item / 2];
-    it.t = s.tile;
-    it.half = item % 2;
-    it.c0 = s.c0;
-    it.nc = s.nc;
-    it.nk1 = it.nk = p.nk_main;
-    it.n = 64 * s.nc;
+    const int si = p.item0 + item / 2;
+    bad = si < 0 || si >= p.plan.n_shrink;
+    if (!bad) {
+      const ShrinkItem s = p.plan.shrink[si];
+      it.t = s.tile;
+      it.half = item % 2;
+      it.c0 = s.c0;
+      it.nc = s.nc;
+      it.nk1 = it.nk = p.nk_main;
+      it.n = 64 * s.nc;
+      bad = s.tile < 0 || s.tile >= p.plan.n_tiles || s.nc < 1 || s.nc > kMaxChunksPerItem || s.c0 < 0 ||
+            s.c0 + s.nc > p.plan.n_chunks;
+    }
   } else {
-    it.ri = p.plan.reduce[item];
-    it.nc = it.ri.nc;
-    it.nk1 = it.nk = 4 * (it.ri.le - it.ri.lb);  // 64-row K slices of 256-row blocks
-    it.n = 64 * it.nc;
-    it.t = 0;
-    it.c0 = 0;
-    it.skip = it.ri.kind == 0 ? (p.dA == nullptr || !p.da_on)
-                              : (p.dB == nullptr || it.ri.block < p.db0 || it.ri.block >= p.db1);
+    bad = item < 0 || item >= p.plan.n_reduce;
+    if (!bad) {
+      it.ri = p.plan.reduce[item];
+      it.nc = it.ri.nc;
+      it.nk1 = it.nk = 4 * (it.ri.le - it.ri.lb);  // 64-row K slices of 256-row blocks
+      it.n = 64 * it.nc;
+      it.skip = it.ri.kind == 0 ? (p.dA == nullptr || !p.da_on)
+                                : (p.dB == nullptr || it.ri.block < p.db0 || it.ri.block >= p.db1);
+      bad = it.ri.nc < 1 || it.ri.nc > kMaxChunksPerItem || it.ri.lb < 0 || it.ri.le > p.plan.n_list ||
+            it.ri.le < it.ri.lb || it.ri.j0 < 0 || it.ri.block < 0;
+    }
+  }
+  if (bad) {
+    atomicOr(&g_err_word, kErrBounds);
+    it.skip = true;
   }
   return it;
 }
@@ -910,6 +937,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
       const int row0 = it.t * kTileRows + int(crank) * kHalfRows;  // this CTA's A rows
       const int nh = it.nb * 256 + int(crank) * 128;               // this CTA's half of the N block
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
@@ -969,6 +997,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(acc * kAccCols);
@@ -1014,6 +1043,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);

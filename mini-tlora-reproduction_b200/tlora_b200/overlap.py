@@ -45,6 +45,24 @@ from ._lib import TILE_ROWS
 from .nano import AIMDController, split_ranges
 
 
+class _Range:
+    """NVTX range (visible in Nsight timelines) around a phase of the step;
+    a no-op without CUDA."""
+
+    def __init__(self, name: str):
+        self.name = name
+        self.on = torch.cuda.is_available()
+
+    def __enter__(self):
+        if self.on:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if self.on:
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
 def shard_columns(d_in: int, rank: int, world: int, align: int = 64) -> Tuple[int, int]:
     """Contiguous column range of d_in owned by ``rank``: near-equal blocks of
     ``align`` columns (keeps every shard's row pitch 16-byte aligned)."""
@@ -164,7 +182,8 @@ class ShardedLayer:
         in flight: (Y, ctx, Y work handles, Z work handle or None)."""
         c = self.compute
         ctx = c.begin(self, x_p, plan)
-        c.shrink(ctx)
+        with _Range("mlora.shrink"):
+            c.shrink(ctx)
         hz = None
         if comm and ctx["z"] is not None:
             hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
@@ -174,15 +193,16 @@ class ShardedLayer:
             hz = None
         rows = x_p.shape[0]
         works = []
-        for t0, t1 in split_ranges(ctx["n_tiles"], n_nano):
-            c.main(ctx, t0, t1, expand=owner, add_bias=owner)
-            if not comm:
-                continue
-            seg = ctx["y"][t0 * TILE_ROWS:min(t1 * TILE_ROWS, rows)]
-            if pipelined:
-                works.append(dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
-            else:
-                dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group)
+        for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
+            with _Range(f"mlora.nano{i}"):
+                c.main(ctx, t0, t1, expand=owner, add_bias=owner)
+                if not comm:
+                    continue
+                seg = ctx["y"][t0 * TILE_ROWS:min(t1 * TILE_ROWS, rows)]
+                if pipelined:
+                    works.append(dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+                else:
+                    dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group)
         return ctx["y"], ctx, works, hz
 
     def backward(self, ctx, x_p, dy, overlapped=False):
@@ -212,8 +232,10 @@ class ShardedLayer:
         y, ctx, works, hz = self.forward_async(x_p, plan, n_nano, pipelined, comm)
         if hz is not None:
             hz.wait()  # dB = dY^T Z needs the summed Z
-        dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works))
-        self.compute.sgd(self, plan, dA_p, dB, lr)
+        with _Range("mlora.backward"):
+            dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works))
+        with _Range("mlora.sgd"):
+            self.compute.sgd(self, plan, dA_p, dB, lr)
         for w in works:
             w.wait()
         return y, dx_p

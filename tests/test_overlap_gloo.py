@@ -179,3 +179,61 @@ def test_nano_ranges_over_tiles():
         for n in [1, 2, 4, 8, 16, 32]:
             r = split_ranges(tiles, n)
             assert r[0][0] == 0 and r[-1][1] == tiles and len(r) == min(n, tiles)
+
+
+# ---------------------------------------------------------------- failure detection
+# A rank that is lost (exits before the step's collectives) or late must not
+# hang the others: the process group carries a short timeout, a lost peer
+# surfaces as an exception on the surviving rank, a late one within the
+# timeout only delays the step.  Host-side only (gloo on CPU): no GPU is
+# faulted or hung to test this.
+
+def _fault_worker(rank, world, port, mode, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    m, ids, x, dy = _build()
+    layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group([0, 1]))
+    plan = ops.route(ids, layer.table, torch.device("cpu"))
+    x_p = layer.shard_input(x)
+    if rank == 1 and mode == "lost":
+        os._exit(0)  # leaves between steps, none of its collectives in flight
+    if rank == 1 and mode == "late":
+        time.sleep(1.5)
+    t0 = time.monotonic()
+    try:
+        layer.step(x_p, plan, dy, 2, lr=0.01)
+        outcome = "ok"
+    except Exception as e:  # noqa: BLE001 - the failure is what is being tested
+        outcome = f"error: {type(e).__name__}"
+    if rank == 0:
+        q.put((outcome, time.monotonic() - t0))
+        q.close()
+        q.join_thread()  # flush before os._exit
+    if outcome == "ok":
+        dist.destroy_process_group()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["lost", "late"])
+def test_lost_or_late_rank(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        outcome, seconds = q.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    if mode == "lost":
+        assert outcome.startswith("error"), outcome  # surfaced, not hung
+        assert seconds < 60
+    else:
+        assert outcome == "ok", outcome
