@@ -284,8 +284,9 @@ def run_single(args, peaks_d, peaks_kind):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for _ in range(args.steps):
-        step_fn()
+    with torch.no_grad() if not sp.train else torch.enable_grad():  # forward-only workloads: inference
+        for _ in range(args.steps):
+            step_fn()
     e1.record(st)
     torch.cuda.synchronize()
     ck = clocks.stop()
