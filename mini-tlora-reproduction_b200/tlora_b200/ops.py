@@ -129,7 +129,8 @@ def route(ids: torch.Tensor, table: AdapterTable, device: torch.device) -> Route
     """Segments for per-row adapter ids.  Ids already grouped (each adapter in
     one contiguous run, the packed layout of the reference's phase3-6 scripts)
     are used in place; interleaved ids are stably sorted by adapter, and the
-    plan carries the permutation that gathers X / scatters Y."""
+    plan carries the permutation that gathers X (and dY) into adapter order
+    and that the kernels use to write Y (and dX) back in the caller's order."""
     rows = int(ids.shape[0])
     n = table.n
     if rows == 0:

@@ -387,3 +387,16 @@ def test_out_rows_outside_the_rows_sets_the_bounds_flag():
     assert _lib.device_error() & 1
     _lib.clear_device_error()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_gather_scatter_rows_round_trip(dtype):
+    """mlora_gather_rows / mlora_scatter_rows (the C ABI's row permutation for
+    callers that do not use out_rows): dst[i] = src[perm[i]] and back."""
+    from tlora_b200 import ops
+    src = torch.randn(1000, 72, device=DEV).to(dtype)
+    perm = torch.randperm(1000, device=DEV).to(torch.int32)
+    g = ops.gather_rows(src, perm)
+    torch.cuda.synchronize()
+    assert torch.equal(g, src[perm.long()])
+    assert torch.equal(ops.scatter_rows(g, perm), src)
