@@ -46,6 +46,7 @@ struct ShrinkItem {
 struct ReduceItem {
   int32_t slot, j0, nc, kind;  // kind 0 = dA, 1 = dB
   int32_t block, lb, le, rank;  // rank = true rank of the adapter
+  int32_t nks;                  // 64-row slices of the adapter's tiles that hold its rows (the K extent)
 };
 
 // Device-side plan header, followed in the workspace by the arrays.

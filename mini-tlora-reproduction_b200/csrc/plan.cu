@@ -116,6 +116,13 @@ int build_plan(const mlora_problem* prob, const mlora_routing* r, Plan* p) {
   for (int a = 0; a < nad; ++a) {
     const int lb = p->list_begin[a], le = p->list_begin[a + 1];
     if (le == lb) continue;
+    // only the 64-row slices of each tile that hold the segment's rows are
+    // summed (the rest of dZt / Zt is zero there)
+    int nks = 0;
+    for (int e = lb; e < le; ++e) {
+      const Chunk& ch = p->chunks[p->list[e]];
+      nks += (ch.hi + 63) / 64 - ch.lo / 64;
+    }
     const int nch = (r->rank[a] + kChunk - 1) / kChunk;
     for (int j0 = 0; j0 < nch; j0 += kMaxChunksPerItem) {
       const int nc = std::min(kMaxChunksPerItem, nch - j0);
@@ -131,14 +138,14 @@ int build_plan(const mlora_problem* prob, const mlora_routing* r, Plan* p) {
           it.lb = lb;
           it.le = le;
           it.rank = r->rank[a];
+          it.nks = nks;
           p->reduce.push_back(it);
         }
       }
     }
   }
-  std::stable_sort(p->reduce.begin(), p->reduce.end(), [](const ReduceItem& x, const ReduceItem& y) {
-    return (x.le - x.lb) > (y.le - y.lb);
-  });
+  std::stable_sort(p->reduce.begin(), p->reduce.end(),
+                   [](const ReduceItem& x, const ReduceItem& y) { return x.nks > y.nks; });
 
   // workspace layout
   size_t off = align_up(sizeof(PlanDev), 256);

@@ -443,12 +443,13 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
     if (!bad) {
       it.ri = p.plan.reduce[item];
       it.nc = it.ri.nc;
-      it.nk1 = it.nk = 4 * (it.ri.le - it.ri.lb);  // 64-row K slices of 256-row blocks
+      it.nk1 = it.nk = it.ri.nks;  // 64-row K slices of the tiles that hold the adapter's rows
       it.n = 64 * it.nc;
       it.skip = it.ri.kind == 0 ? (p.dA == nullptr || !p.da_on)
                                 : (p.dB == nullptr || it.ri.block < p.db0 || it.ri.block >= p.db1);
       bad = it.ri.nc < 1 || it.ri.nc > kMaxChunksPerItem || it.ri.lb < 0 || it.ri.le > p.plan.n_list ||
-            it.ri.le < it.ri.lb || it.ri.j0 < 0 || it.ri.block < 0;
+            it.ri.le < it.ri.lb || it.ri.j0 < 0 || it.ri.block < 0 || it.ri.nks < 0 ||
+            it.ri.nks > 4 * (it.ri.le - it.ri.lb);
     }
   }
   if (bad) {
@@ -456,6 +457,20 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
     it.skip = true;
   }
   return it;
+}
+
+// REDUCE: list entry e of a reduce item -> its base chunk, tile and the range
+// [q, q1) of 64-row slices of the tile that hold the segment's rows
+__device__ __forceinline__ void reduce_entry(const TcParams& p, int e, int& cb, int& t, int& q, int& q1) {
+  cb = p.plan.list[e];
+  if (cb < 0 || cb >= p.plan.n_chunks) {  // corrupted plan: flag it, load tile 0 instead of out of bounds
+    atomicOr(&g_err_word, kErrBounds);
+    cb = 0;
+  }
+  const Chunk ch = p.plan.chunks[cb];
+  t = ch.tile;
+  q = ch.lo / 64;
+  q1 = (ch.hi + 63) / 64;
 }
 
 // ------------------------------------------------------------------ tile scheduler
@@ -652,6 +667,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       if (it.skip) continue;
       const int row0 = it.t * kTileRows + it.half * kHalfRows;  // first X / dY row of the A tile
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
+      int r_e = 0, r_cb = 0, r_t = 0, r_q = 0, r_q1 = 0;  // REDUCE: list entry, chunk, tile, slice range
+      if (MODE == REDUCE) {
+        r_e = it.ri.lb;
+        if (it.nk > 0) reduce_entry(p, r_e, r_cb, r_t, r_q, r_q1);
+      }
       for (int kb = 0; kb < it.nk; ++kb) {
         if (kb == claim_kb) claimed = atomicAdd(p.counter, 1);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
@@ -690,17 +710,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
           tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
           for (int i = 0; i < it.nc; ++i)
             tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64, pol_keep);
-        } else {  // REDUCE: k-block kb = 64-row slice q of list entry kb / 4
-          const int cb = p.plan.list[it.ri.lb + kb / 4];
-          const int q = kb % 4;
-          const int t = p.plan.chunks[cb].tile;
+        } else {  // REDUCE: k-block kb = slice r_q of list entry r_e
           const CUtensorMap* ma = it.ri.kind == 0 ? &p.mA0 : &p.mA1;
           const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
           mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
           for (int i = 0; i < 2; ++i)
-            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, t * kTileRows + 64 * q, pol_stream);
+            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, r_t * kTileRows + 64 * r_q, pol_stream);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, mb, bar, 0, (cb + it.ri.j0 + i) * kTileRows + 64 * q, pol_norm);
+            tma_load(sB + i * kBox64, mb, bar, 0, (r_cb + it.ri.j0 + i) * kTileRows + 64 * r_q, pol_norm);
+          if (++r_q >= r_q1 && ++r_e < it.ri.le) reduce_entry(p, r_e, r_cb, r_t, r_q, r_q1);
         }
         issued |= 1u << stage;
         issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
