@@ -30,6 +30,7 @@ int upload_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
   put(p.off_shrink, p.shrink.data(), sizeof(ShrinkItem) * p.shrink.size());
   put(p.off_reduce, p.reduce.data(), sizeof(ReduceItem) * p.reduce.size());
   put(p.off_list, p.list.data(), sizeof(int32_t) * p.list.size());
+  put(p.off_list_desc, p.list_desc.data(), sizeof(int4) * p.list_desc.size());
   MLORA_CUDA_TRY(cudaMemcpyAsync(ws, host.data(), p.bytes, cudaMemcpyHostToDevice, st));
   uint8_t* b = (uint8_t*)ws;
   std::memset(dev, 0, sizeof(*dev));
@@ -43,6 +44,7 @@ int upload_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
   dev->shrink = (const ShrinkItem*)(b + p.off_shrink);
   dev->reduce = (const ReduceItem*)(b + p.off_reduce);
   dev->list = (const int32_t*)(b + p.off_list);
+  dev->list_desc = (const int4*)(b + p.off_list_desc);
   dev->counters = (int32_t*)(b + p.off_counters);
   return MLORA_OK;
 }

@@ -58,6 +58,7 @@ struct PlanDev {
   const ShrinkItem* shrink;         // [n_shrink]
   const ReduceItem* reduce;         // [n_reduce]
   const int32_t* list;              // [n_list] base chunk ids, grouped by adapter
+  const int4* list_desc;            // [n_list] {base chunk, tile, first 64-row slice, one past the last}
   int32_t* counters;                // [16] work counters of the persistent kernels, one per role;
                                     // zeroed by every plan upload (one per API call)
 };
@@ -71,10 +72,11 @@ struct Plan {
   std::vector<ShrinkItem> shrink;
   std::vector<ReduceItem> reduce;
   std::vector<int32_t> list;
+  std::vector<int4> list_desc;      // per list entry: {base chunk, tile, first slice, end slice}
   std::vector<int32_t> list_begin;  // [n_adapters + 1]
   std::vector<uint8_t> adapter_active;
   // byte layout of the plan inside the workspace
-  size_t off_tcb = 0, off_chunks = 0, off_shrink = 0, off_reduce = 0, off_list = 0,
+  size_t off_tcb = 0, off_chunks = 0, off_shrink = 0, off_reduce = 0, off_list = 0, off_list_desc = 0,
          off_counters = 0, bytes = 0;
 };
 

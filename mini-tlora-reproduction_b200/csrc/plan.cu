@@ -109,6 +109,11 @@ int build_plan(const mlora_problem* prob, const mlora_routing* r, Plan* p) {
       p->list.insert(p->list.end(), per[a].begin(), per[a].end());
     }
     p->list_begin[nad] = int32_t(p->list.size());
+    p->list_desc.resize(p->list.size());
+    for (size_t e = 0; e < p->list.size(); ++e) {
+      const Chunk& ch = p->chunks[p->list[e]];
+      p->list_desc[e] = make_int4(p->list[e], ch.tile, ch.lo / 64, (ch.hi + 63) / 64);
+    }
   }
 
   // reduction items (dA over d_in blocks, dB over d_out blocks), longest first
@@ -159,6 +164,8 @@ int build_plan(const mlora_problem* prob, const mlora_routing* r, Plan* p) {
   off = align_up(off + sizeof(ReduceItem) * p->reduce.size(), 256);
   p->off_list = off;
   off = align_up(off + sizeof(int32_t) * p->list.size(), 256);
+  p->off_list_desc = off;
+  off = align_up(off + sizeof(int4) * p->list_desc.size(), 256);
   p->off_counters = off;
   off = align_up(off + 64, 256);
   p->bytes = off;

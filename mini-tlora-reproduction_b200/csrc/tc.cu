@@ -459,18 +459,16 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
   return it;
 }
 
-// REDUCE: list entry e of a reduce item -> its base chunk, tile and the range
-// [q, q1) of 64-row slices of the tile that hold the segment's rows
-__device__ __forceinline__ void reduce_entry(const TcParams& p, int e, int& cb, int& t, int& q, int& q1) {
-  cb = p.plan.list[e];
-  if (cb < 0 || cb >= p.plan.n_chunks) {  // corrupted plan: flag it, load tile 0 instead of out of bounds
+// REDUCE: list entry e of a reduce item -> {base chunk, tile, first slice,
+// end slice} (the 64-row slices of the tile that hold the segment's rows), one
+// 16-byte load; out-of-range values (a corrupted plan) are flagged and clamped
+__device__ __forceinline__ int4 reduce_entry(const TcParams& p, int e) {
+  int4 d = p.plan.list_desc[e];
+  if (d.x < 0 || d.x >= p.plan.n_chunks || d.y < 0 || d.y >= p.plan.n_tiles || d.z < 0 || d.w > 4 || d.z > d.w) {
     atomicOr(&g_err_word, kErrBounds);
-    cb = 0;
+    d = make_int4(0, 0, 0, 0);
   }
-  const Chunk ch = p.plan.chunks[cb];
-  t = ch.tile;
-  q = ch.lo / 64;
-  q1 = (ch.hi + 63) / 64;
+  return d;
 }
 
 // ------------------------------------------------------------------ tile scheduler
@@ -667,11 +665,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       if (it.skip) continue;
       const int row0 = it.t * kTileRows + it.half * kHalfRows;  // first X / dY row of the A tile
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
-      int r_e = 0, r_cb = 0, r_t = 0, r_q = 0, r_q1 = 0;  // REDUCE: list entry, chunk, tile, slice range
-      if (MODE == REDUCE) {
+      // REDUCE: current list entry r_e with its descriptor (r_d: chunk, tile, slice
+      // range; r_q the current slice) and the next entry's descriptor, loaded one
+      // entry ahead so its latency hides behind the current entry's loads
+      int r_e = 0, r_q = 0;
+      int4 r_d = make_int4(0, 0, 0, 0), r_n = make_int4(0, 0, 0, 0);
+      if (MODE == REDUCE && it.nk > 0) {
         r_e = it.ri.lb;
-        if (it.nk > 0) reduce_entry(p, r_e, r_cb, r_t, r_q, r_q1);
+        r_d = reduce_entry(p, r_e);
+        r_q = r_d.z;
+        if (r_e + 1 < it.ri.le) r_n = reduce_entry(p, r_e + 1);
       }
+
       for (int kb = 0; kb < it.nk; ++kb) {
         if (kb == claim_kb) claimed = atomicAdd(p.counter, 1);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
@@ -715,10 +720,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
           const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
           mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
           for (int i = 0; i < 2; ++i)
-            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, r_t * kTileRows + 64 * r_q, pol_stream);
+            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, r_d.y * kTileRows + 64 * r_q, pol_stream);
           for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, mb, bar, 0, (r_cb + it.ri.j0 + i) * kTileRows + 64 * r_q, pol_norm);
-          if (++r_q >= r_q1 && ++r_e < it.ri.le) reduce_entry(p, r_e, r_cb, r_t, r_q, r_q1);
+            tma_load(sB + i * kBox64, mb, bar, 0, (r_d.x + it.ri.j0 + i) * kTileRows + 64 * r_q, pol_norm);
+          if (++r_q >= r_d.w && ++r_e < it.ri.le) {
+            r_d = r_n;
+            r_q = r_d.z;
+            if (r_e + 1 < it.ri.le) r_n = reduce_entry(p, r_e + 1);
+          }
         }
         issued |= 1u << stage;
         issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
