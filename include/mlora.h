@@ -80,7 +80,14 @@ typedef struct mlora_problem {
                        0 = one per SM.  A smaller value leaves SMs free for
                        communication kernels running at the same time (the
                        nano-batch all-reduce overlap). */
+  int32_t flags;    /* MLORA_PLAN_* below; 0 by default */
 } mlora_problem;
+/* flags: the workspace already holds this problem's routing plan, written by
+ * mlora_plan_upload with the same problem and routing; the call then issues
+ * no host->device copy (only a device-side reset of its work counters), so a
+ * sequence of calls can be captured into a CUDA graph and replayed.  The
+ * caller keeps the workspace untouched between the upload and the calls. */
+#define MLORA_PLAN_RESIDENT 1
 
 typedef struct mlora_routing {
   int32_t n_seg;              /* number of contiguous row segments */
@@ -106,6 +113,11 @@ int mlora_zsave_bytes(const mlora_problem* prob, const mlora_routing* route, siz
 
 /* Bytes of scratch workspace needed by mlora_forward / mlora_backward. */
 int mlora_workspace_bytes(const mlora_problem* prob, const mlora_routing* route, size_t* bytes);
+/* Write the routing plan of (prob, route) into the workspace (one host->device
+ * copy on `stream`) for later calls with MLORA_PLAN_RESIDENT.  No counterpart
+ * in the reference (which has no plan); it replaces nothing. */
+int mlora_plan_upload(const mlora_problem* prob, const mlora_routing* route, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* Fused forward: Y = X W^T + bias + per-segment LoRA.  bias may be NULL.
  * W may be NULL: then only the LoRA delta (+ bias) is computed, the

@@ -49,6 +49,32 @@ int upload_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
   return MLORA_OK;
 }
 
+// Device view of a plan already in the workspace (MLORA_PLAN_RESIDENT): no
+// copy; the per-launch work counters are reset on the stream.
+int view_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
+  uint8_t* b = (uint8_t*)ws;
+  std::memset(dev, 0, sizeof(*dev));
+  dev->n_tiles = p.n_tiles;
+  dev->n_chunks = int32_t(p.chunks.size());
+  dev->n_shrink = int32_t(p.shrink.size());
+  dev->n_reduce = int32_t(p.reduce.size());
+  dev->n_list = int32_t(p.list.size());
+  dev->tile_chunk_begin = (const int32_t*)(b + p.off_tcb);
+  dev->chunks = (const Chunk*)(b + p.off_chunks);
+  dev->shrink = (const ShrinkItem*)(b + p.off_shrink);
+  dev->reduce = (const ReduceItem*)(b + p.off_reduce);
+  dev->list = (const int32_t*)(b + p.off_list);
+  dev->list_desc = (const int4*)(b + p.off_list_desc);
+  dev->counters = (int32_t*)(b + p.off_counters);
+  MLORA_CUDA_TRY(cudaMemsetAsync(dev->counters, 0, p.bytes - p.off_counters, st));
+  return MLORA_OK;
+}
+
+// Plan of a call: uploaded now, or already resident in the workspace.
+int stage_plan(const mlora_problem* prob, const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
+  return (prob->flags & MLORA_PLAN_RESIDENT) ? view_plan(p, ws, st, dev) : upload_plan(p, ws, st, dev);
+}
+
 bool tc_shape_ok(const mlora_problem* prob) {
   // TMA: global strides must be multiples of 16 bytes (bf16: 8 elements)
   return (prob->dtype == MLORA_BF16 || prob->dtype == MLORA_F16) && prob->d_in % 8 == 0 && prob->d_out % 8 == 0;
@@ -85,6 +111,17 @@ extern "C" int mlora_workspace_bytes(const mlora_problem* prob, const mlora_rout
   return MLORA_OK;
 }
 
+extern "C" int mlora_plan_upload(const mlora_problem* prob, const mlora_routing* route, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  Plan p;
+  int st = build_plan(prob, route, &p);
+  if (st != MLORA_OK) return st;
+  if (!workspace) return MLORA_ERR_INVALID_ARG;
+  if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
+  PlanDev dev;
+  return upload_plan(p, workspace, (cudaStream_t)stream, &dev);
+}
+
 extern "C" int32_t mlora_num_tiles(int64_t rows) {
   return rows <= 0 ? 0 : int32_t((rows + kTileRows - 1) / kTileRows);
 }
@@ -113,7 +150,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
   PlanDev dev;
-  st = upload_plan(p, workspace, s, &dev);
+  st = stage_plan(prob, p, workspace, s, &dev);
   if (st != MLORA_OK) return st;
   if (impl == MLORA_IMPL_TC) {
     TcCall a;
@@ -180,7 +217,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
   PlanDev dev;
-  st = upload_plan(p, workspace, s, &dev);
+  st = stage_plan(prob, p, workspace, s, &dev);
   if (st != MLORA_OK) return st;
   if (impl == MLORA_IMPL_TC) {
     TcCall a;

@@ -76,6 +76,8 @@ extern "C" int mlora_forward_noalloc(const mlora_problem* prob, const mlora_rout
   st = noalloc_scratch(&base);
   if (st != MLORA_OK) return st;
   unsigned char* b = static_cast<unsigned char*>(base);
-  return mlora_forward(prob, route, X, W, bias, A_pack, B_pack, Y, zbytes ? b + zoff : nullptr, b,
-                       wbytes, stream);
+  mlora_problem q = *prob;
+  q.flags = 0;  // the shared scratch never keeps a plan between calls
+  return mlora_forward(&q, route, X, W, bias, A_pack, B_pack, Y, zbytes ? b + zoff : nullptr, b, wbytes,
+                       stream);
 }

@@ -47,6 +47,9 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <mutex>
+#include <utility>
+#include <vector>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -1151,6 +1154,23 @@ int cta_budget(int max_ctas) {
   return sms;
 }
 
+// Dynamic shared memory opt-in of a kernel, once per kernel and device (not
+// on every launch, so that launches can be captured into a CUDA graph).
+cudaError_t set_smem_once(const void* fn, int bytes) {
+  constexpr int kDevs = 64;
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && done.size() < size_t(kDevs) * 16) done.emplace_back(fn, dev);
+  return e;
+}
+
 // Ring of a 1-SM launch whose stages hold `a_bytes` of A and at most
 // `b_bytes` of B.
 void set_ring(TcParams& prm, int a_bytes, int b_bytes) {
@@ -1166,7 +1186,7 @@ int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
     return MLORA_ERR_INVALID_ARG;
   const int sms = cta_budget(max_ctas);
   if (sms <= 0) return MLORA_ERR_CUDA;
-  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem1));
+  MLORA_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(&k_tc<MODE>), kSmem1));
   prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
   const int grid = prm.n_items < sms ? prm.n_items : sms;
   cudaEvent_t ev[2] = {nullptr, nullptr};
@@ -1182,7 +1202,7 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
   if (prm.n_items <= 0) return MLORA_OK;
   const int sms = cta_budget(max_ctas);
   if (sms < 2) return MLORA_ERR_UNSUPPORTED;
-  MLORA_CUDA_TRY(cudaFuncSetAttribute(k_tc2<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
+  MLORA_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(&k_tc2<MODE>), kSmem2));
   prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
   const int pairs = std::min(prm.n_items, sms / 2);
   cudaEvent_t ev[2] = {nullptr, nullptr};

@@ -28,6 +28,7 @@ ERR_TIMEOUT = 6
 F32 = 0
 BF16 = 1
 F16 = 2
+PLAN_RESIDENT = 1  # mlora_problem.flags
 
 RANK_CHUNK = 64
 TILE_ROWS = 256
@@ -59,6 +60,7 @@ class Problem(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("impl", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 
@@ -92,6 +94,7 @@ _VP = ctypes.c_void_p
 SIGNATURES = {
     "mlora_zsave_bytes": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), ctypes.POINTER(ctypes.c_size_t)]),
     "mlora_workspace_bytes": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), ctypes.POINTER(ctypes.c_size_t)]),
+    "mlora_plan_upload": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, ctypes.c_size_t, _VP]),
     "mlora_forward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,
                                      _VP, _VP, _VP, ctypes.c_size_t, _VP]),
     "mlora_forward_staged": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,

@@ -205,6 +205,18 @@ class MultiLoRALinear(nn.Module):
         dev = torch.device(device) if device is not None else self.base.weight.device
         return ops.route(adapter_ids, self._pack().table, dev)
 
+    def make_resident(self, plan: ops.RoutePlan) -> None:
+        """Upload the routing ``plan`` once into a device workspace kept on the
+        plan; calls with ``plan=plan`` then issue no host-to-device copy, so a
+        training step with fixed routing can be captured into a CUDA graph
+        (tlora_b200.graphs.GraphedTrainStep).  The adapters' ranks and
+        scalings must not change afterwards."""
+        pk = self._pack()
+        pk.sync()
+        st = ops.LayerState(pk.table, pk.scaling(), plan, pk.A_pack, pk.B_pack, self.impl)
+        w = self.base.weight
+        ops.make_resident(st, plan.rows, self.base.in_features, self.base.out_features, w.dtype, w.device)
+
     def packed(self):
         """(A_pack, B_pack, AdapterTable): the packed adapter storage."""
         p = self._pack()

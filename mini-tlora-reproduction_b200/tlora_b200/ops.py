@@ -93,6 +93,9 @@ class RoutePlan:
     seg_adapter: np.ndarray  # int32 [n_seg], slot or -1
     perm: Optional[torch.Tensor] = None  # int32 [rows] on device: sorted position -> source row
     active: np.ndarray = None            # bool [n_adapters]: adapter owns >= 1 row
+    # workspaces that already hold this plan on the device (make_resident),
+    # keyed by the call shape; calls with such a key upload nothing
+    resident: dict = field(default_factory=dict)
 
     @property
     def n_seg(self) -> int:
@@ -205,8 +208,8 @@ class _CallArgs:
     """Keeps the numpy arrays behind the ctypes structs alive for one call."""
 
     def __init__(self, rows, d_in, d_out, dtype, impl, plan: RoutePlan, table: AdapterTable,
-                 scaling: np.ndarray, max_ctas: int = 0, out_rows: Optional[torch.Tensor] = None):
-        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas))
+                 scaling: np.ndarray, max_ctas: int = 0, out_rows: Optional[torch.Tensor] = None, flags: int = 0):
+        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas), int(flags))
         self.seg_start = np.ascontiguousarray(plan.seg_start, dtype=np.int32)
         self.seg_adapter = np.ascontiguousarray(plan.seg_adapter, dtype=np.int32)
         self.rank = np.ascontiguousarray(table.rank, dtype=np.int32)
@@ -239,6 +242,39 @@ class LayerState:
     max_ctas: int = 0  # cap on persistent-kernel CTAs (0 = one per SM)
 
 
+def _resident_key(rows, d_in, d_out, dtype, st: LayerState):
+    return (int(rows), int(d_in), int(d_out), int(dtype), st.impl, int(st.table.r_pack))
+
+
+def make_resident(st: LayerState, rows: int, d_in: int, d_out: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """Upload the routing plan of ``st`` for calls of this shape into a
+    workspace kept on the plan (mlora_plan_upload); later forward / backward
+    calls with the same plan and shape then issue no host-to-device copy
+    (MLORA_PLAN_RESIDENT), which lets a training step be captured into a
+    CUDA graph.  The plan must not change afterwards (same ids, ranks and
+    scalings)."""
+    code = mlora_dtype(dtype)
+    key = _resident_key(rows, d_in, d_out, code, st)
+    if key in st.plan.resident:
+        return st.plan.resident[key]
+    args = _CallArgs(rows, d_in, d_out, code, st.impl, st.plan, st.table, st.scaling)
+    _, wb = args.sizes()
+    ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=device)
+    _lib.call("mlora_plan_upload", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(ws), wb, _stream(device))
+    st.plan.resident[key] = ws
+    return ws
+
+
+def _workspace(st: LayerState, args, wb, device):
+    """(workspace, flags) of a call: the plan's resident workspace when there
+    is one for this shape, else a fresh one the call uploads the plan into."""
+    p = args.prob
+    ws = st.plan.resident.get(_resident_key(p.rows, p.d_in, p.d_out, p.dtype, st))
+    if ws is not None and ws.numel() >= wb and ws.device == device:
+        return ws, _lib.PLAN_RESIDENT
+    return torch.empty(max(wb, 1), dtype=torch.uint8, device=device), 0
+
+
 def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     """Run mlora_forward; returns (Y in the caller's row order, zsave, x in
     sorted order, call args).  With interleaved ids the rows of X are
@@ -253,7 +289,7 @@ def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     dev = x.device
     y = torch.empty(rows, d_out, dtype=x.dtype, device=dev)
     z = torch.empty(max(zb, 1), dtype=torch.uint8, device=dev)
-    ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+    ws, args.prob.flags = _workspace(st, args, wb, dev)
     _lib.call("mlora_forward", ctypes.byref(args.prob), ctypes.byref(args.route), _ptr(xs), _ptr(W), _ptr(bias),
               _ptr(st.A_pack), _ptr(st.B_pack), _ptr(y), _ptr(z), _ptr(ws), wb, _stream(dev))
     return y, z, xs, args
@@ -313,7 +349,7 @@ def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, wan
     args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
                      out_rows=st.plan.perm)
     _, wb = args.sizes()
-    ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+    ws, args.prob.flags = _workspace(st, args, wb, dev)
     dx = torch.empty(rows, d_in, dtype=dy.dtype, device=dev) if want_dx else None
     # every rank row / column of an adapter that owns rows is written; the
     # rest is never exposed (inactive adapters get None gradients)
