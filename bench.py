@@ -356,10 +356,7 @@ def run_single(args, peaks_d, peaks_kind):
         "metric": METRIC, "value": round(tokens_s, 1), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; random-init weights)",
-        "config": {"workload": f"{sp.name}: {'fwd+bwd+isolated SGD' if sp.train else 'fwd'} "
-                               f"d_in={sp.d_in} d_out={sp.d_out} adapters={len(sp.ranks)} ranks={sorted(set(sp.ranks))}",
-                   "rows": rows, "global_batch": rows, "seq_len": None, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (X 512 MiB)"},
+        "config": workload_config(sp),
         "step_tflops": round(step_flops / (ms / 1000.0) / 1e12, 1),
         "step_frac_of_peak": round(step_flops / (ms / 1000.0) / 1e12 /
                                    float(peaks_d.get("bf16_tflops_sustained", 1370.6)), 4),
@@ -379,6 +376,15 @@ def run_single(args, peaks_d, peaks_kind):
     return out
 
 
+def workload_config(sp):
+    """The `config` of the single-GPU line (shared by the reference arm)."""
+    x_mib = sp.rows * sp.d_in * 2 / 2**20
+    return {"workload": f"{sp.name}: {'fwd+bwd+isolated SGD' if sp.train else 'fwd'} "
+                        f"d_in={sp.d_in} d_out={sp.d_out} adapters={len(sp.ranks)} ranks={sorted(set(sp.ranks))}",
+            "rows": sp.rows, "global_batch": sp.rows, "seq_len": None, "parallelism": "single GPU",
+            "l2": f"inputs larger than L2 (X {x_mib:.0f} MiB)" if x_mib > 126 else f"X {x_mib:.0f} MiB"}
+
+
 def run_reference(args):
     """CPU reference arm: the oracle port of the reference's MultiLoRALinear
     (fp32, all host threads) on a bounded sample per step."""
@@ -392,7 +398,7 @@ def run_reference(args):
     return {
         "metric": METRIC, "value": round(tps, 1), "unit": UNIT, "n_gpus": 0, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "impl": "reference", "dtype": "f32",
-        "data": "synthetic (seeded)", "config": {"workload": sp.name, "rows": sp.rows},
+        "data": "synthetic (seeded)", "config": workload_config(sp),
         "cpu_baseline": {"value": round(tps, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": smp},
         "e2e": {"value": round(tps, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "vs_baseline": None,
