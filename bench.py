@@ -298,14 +298,18 @@ def run_single(args, peaks_d, peaks_kind):
     # end to end through the module API: every step copies its X from pinned
     # host memory (on a copy stream, double-buffered so the copy of step i+1
     # overlaps the compute of step i, as a data loader's prefetch does) and
-    # reads a probe of the updated adapter weights back to the host
+    # reads a probe of the updated adapter weights back to the host, waited
+    # for one step later (as a training loop logs its loss), so that the host
+    # queues step i+1 while step i runs; the last read is waited for inside the
+    # timed region
     x_host = w.x.detach().cpu().pin_memory()
     ids_host = w.ids.cpu()
     bufs = [torch.empty_like(w.x.detach()) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     copy_stream = torch.cuda.Stream(dev)
-    probe = torch.empty(64, dtype=w.x.dtype).pin_memory()
+    probes = [torch.empty(64, dtype=w.x.dtype).pin_memory() for _ in range(2)]
+    read = [torch.cuda.Event() for _ in range(2)]
     a0 = m.adapters["0"].A
     compute = torch.cuda.current_stream(dev)
 
@@ -325,9 +329,12 @@ def run_single(args, peaks_d, peaks_kind):
             with torch.no_grad():
                 m(xi, ids_host)
         consumed[i % 2].record(compute)
-        probe.copy_(a0.detach()[0, :64], non_blocking=True)
-        compute.synchronize()
-        return float(probe[0])
+        probes[i % 2].copy_(a0.detach()[0, :64], non_blocking=True)
+        read[i % 2].record(compute)
+        if i > 0:  # the previous step's result
+            read[(i - 1) % 2].synchronize()
+            return float(probes[(i - 1) % 2][0])
+        return None
 
     for ev in consumed:
         ev.record(compute)
@@ -339,6 +346,7 @@ def run_single(args, peaks_d, peaks_kind):
     t0 = time.perf_counter()
     for i in range(2, 2 + n_e2e):
         e2e_step(i)
+    read[(1 + n_e2e) % 2].synchronize()  # the last step's result
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / n_e2e
     torch.cuda.synchronize()
 
@@ -365,7 +373,7 @@ def run_single(args, peaks_d, peaks_kind):
         "kernels_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in kinds.items()},
         "e2e": {"value": round(rows / (e2e_ms / 1000.0), 1), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": int(w.x.numel() * w.x.element_size()),
-                "d2h_bytes_per_step": int(probe.numel() * probe.element_size())},
+                "d2h_bytes_per_step": int(probes[0].numel() * probes[0].element_size())},
         "gpu_launches": int(launches),
         "clocks": ck,
         "cublas_backbone": cublas,

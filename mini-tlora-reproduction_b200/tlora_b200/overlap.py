@@ -311,13 +311,15 @@ def _job_parallel(args, rank, world, dev, metric, unit):
     ms = _timed(step, args.steps, dev)
     launches = _lib.launch_count() - launches0
     # e2e: prefetched pinned H2D of this rank's X, probe read back every step
+    # (waited for one step later; the last one before the closing event)
     x_host = w.x.detach().cpu().pin_memory()
     bufs = [torch.empty_like(w.x.detach()) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     copy_stream = torch.cuda.Stream(dev)
     compute = torch.cuda.current_stream(dev)
-    probe = torch.empty(64, dtype=w.x.dtype).pin_memory()
+    probes = [torch.empty(64, dtype=w.x.dtype).pin_memory() for _ in range(2)]
+    read = [torch.cuda.Event() for _ in range(2)]
     a0 = m.adapters["0"].A
     counter = [0]
 
@@ -334,8 +336,10 @@ def _job_parallel(args, rank, world, dev, metric, unit):
         issue_copy(i + 1)
         step(bufs[i % 2].detach().requires_grad_(True))
         consumed[i % 2].record(compute)
-        probe.copy_(a0.detach()[0, :64], non_blocking=True)
-        compute.synchronize()
+        probes[i % 2].copy_(a0.detach()[0, :64], non_blocking=True)
+        read[i % 2].record(compute)
+        if i > 0:  # the previous step's result, one step late as a training loop logs it
+            read[(i - 1) % 2].synchronize()
 
     for ev in consumed:
         ev.record(compute)
@@ -344,7 +348,7 @@ def _job_parallel(args, rank, world, dev, metric, unit):
     e2e_ms = _timed(e2e, max(3, args.steps // 2), dev)
     torch.cuda.synchronize(dev)
     out = {"sp": sp, "ms": ms, "e2e_ms": e2e_ms, "launches": launches,
-           "h2d": int(w.x.numel() * w.x.element_size()), "d2h": int(probe.numel() * probe.element_size())}
+           "h2d": int(w.x.numel() * w.x.element_size()), "d2h": int(probes[0].numel() * probes[0].element_size())}
     del w, m, x, bufs
     torch.cuda.empty_cache()
     return out
