@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     for (int q = 0; q < kSched; ++q) {
@@ -868,8 +868,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
           }
         }
       }
+      // the accumulator is free once every lane's tcgen05.ld has completed:
+      // fence, then one arrival per warp
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -916,7 +919,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 256);  // both CTAs' epilogue threads
+      mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
     for (int q = 0; q < kSched; ++q) {
@@ -1087,7 +1090,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
         ++slices;
       }
       tc_fence_before();
-      mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);  // one remote arrival per warp
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
