@@ -105,6 +105,8 @@ struct TcParams {
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
   int* counter;     // work-item counter of this launch (zero at launch)
+  int pdl_wait;     // main modes: launched to overlap the shrink before it (programmatic dependent
+                    // launch): wait for it before reading the low-rank intermediate
   const int32_t* out_rows;  // main modes: output row of each (sorted) input row, or nullptr
   int n_stages;     // 1-SM kernel: stages of the ring (<= kMaxStages1)
   int stage_bytes;  // 1-SM kernel: bytes per stage (multiple of 8 KB)
@@ -259,6 +261,11 @@ __device__ __forceinline__ void tma_store(const CUtensorMap* map, uint32_t src, 
                "r"(x), "r"(y)
                : "memory");
 }
+// Programmatic dependent launch: a shrink lets the mainloop after it start on
+// the SMs its last work items leave idle; the mainloop waits for the shrink's
+// completion (and memory) only before its first read of the intermediate.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -651,8 +658,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) grid_dep_launch();  // the mainloop after it may start
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA producer
+    bool dep_done = !p.pdl_wait;  // the shrink before this launch is known complete
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
@@ -686,6 +695,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         uint8_t* sA = smem + stage * stage_bytes;
         uint8_t* sB = sA + kA1Bytes;
         uint64_t* bar = &full[stage];
+        if ((MODE == FWD_MAIN || MODE == DX_MAIN) && kb >= it.nk1 && !dep_done) {
+          grid_dep_wait();  // the intermediate is the shrink's output
+          dep_done = true;
+        }
         if (MODE == FWD_MAIN) {
           mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
           if (kb < it.nk1) {
@@ -737,6 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         if (++stage == n_stages) { stage = 0; phase ^= 1; }
       }
     }
+    if (!dep_done) grid_dep_wait();  // never finish before the shrink this launch overlaps
     if (!ok) {
       // let copies already in flight land before the CTA exits
       const unsigned long long t0 = now_ns();
@@ -943,6 +957,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
+    bool dep_done = !p.pdl_wait;  // the shrink before this launch is known complete
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
@@ -980,6 +995,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
         uint8_t* sA = smem + stage * kStage2Bytes;
         uint8_t* sB = sA + kA2Bytes;
         const uint32_t bar = mapa(su32(&full[stage]), 0);  // the even CTA's barrier
+        if (kb >= it.nk1 && !dep_done) {
+          grid_dep_wait();  // the intermediate is the shrink's output
+          dep_done = true;
+        }
         if (leader) mbar_expect_tx(&full[stage], 2 * kStage2Bytes);
         if (kb < it.nk1) {
           tma_load_pair(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
@@ -1003,6 +1022,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
         if (++stage == kStages2) { stage = 0; phase ^= 1; }
       }
     }
+    if (!dep_done) grid_dep_wait();  // never finish before the shrink this launch overlaps
     if (!ok && leader) {
       const unsigned long long t0 = now_ns();
       for (int s = 0; s < kStages2; ++s) {
@@ -1182,8 +1202,32 @@ void set_ring(TcParams& prm, int a_bytes, int b_bytes) {
   prm.n_stages = std::min(kMaxStages1, kRing1Bytes / prm.stage_bytes);
 }
 
+// Programmatic dependent launches are on unless MLORA_NO_PDL is set (for
+// A/B timing and debugging).
+bool pdl_enabled() {
+  static const bool on = std::getenv("MLORA_NO_PDL") == nullptr;
+  return on;
+}
+
+// Launch `kern` on `st`; with `pdl`, as a programmatic dependent launch of the
+// kernel before it in the stream (it may start while that one finishes).
+template <class K>
+cudaError_t launch_k(K kern, dim3 grid, int smem, cudaStream_t st, bool pdl, const TcParams& prm) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, prm);
+}
+
 template <int MODE>
-int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
+int launch1(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   if (prm.n_items <= 0) return MLORA_OK;
   if (prm.n_stages < 2 || prm.n_stages > kMaxStages1 || prm.stage_bytes % 1024 != 0 ||
       prm.n_stages * prm.stage_bytes > kRing1Bytes)
@@ -1195,14 +1239,16 @@ int launch1(TcParams& prm, cudaStream_t st, int max_ctas) {
   const int grid = prm.n_items < sms ? prm.n_items : sms;
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);
-  k_tc<MODE><<<grid, kThreads, kSmem1, st>>>(prm);
+  if (timed || !pdl_enabled()) pdl = false;  // events between the launches order them anyway
+  prm.pdl_wait = pdl ? 1 : 0;
+  MLORA_CUDA_TRY(launch_k(k_tc<MODE>, dim3(grid), kSmem1, st, pdl, prm));
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
 }
 
 template <int MODE>
-int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
+int launch2(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   if (prm.n_items <= 0) return MLORA_OK;
   const int sms = cta_budget(max_ctas);
   if (sms < 2) return MLORA_ERR_UNSUPPORTED;
@@ -1211,7 +1257,9 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas) {
   const int pairs = std::min(prm.n_items, sms / 2);
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);
-  k_tc2<MODE><<<2 * pairs, kThreads, kSmem2, st>>>(prm);
+  if (timed || !pdl_enabled()) pdl = false;  // events between the launches order them anyway
+  prm.pdl_wait = pdl ? 1 : 0;
+  MLORA_CUDA_TRY(launch_k(k_tc2<MODE>, dim3(2 * pairs), kSmem2, st, pdl, prm));
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -1275,6 +1323,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
   const int64_t zrows = int64_t(n_chunks) * kTileRows;
   if (a.t1 <= a.t0) return MLORA_OK;
+  bool after_shrink = false;  // the shrink was launched just before: the mainloop may overlap its tail
   if (n_chunks > 0 && (a.stages & MLORA_STAGE_SHRINK)) {
     // shrink items are in tile order: the launch covers those of [t0, t1)
     const std::vector<ShrinkItem>& sh = a.host->shrink;
@@ -1290,6 +1339,7 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.zsave);
     int s = launch1<SHRINK_FWD>(prm, st, a.max_ctas);
     if (s != MLORA_OK) return s;
+    after_shrink = prm.n_items > 0;
   }
   if (!(a.stages & MLORA_STAGE_MAIN)) return MLORA_OK;
   const bool expand = n_chunks > 0 && !(a.stages & MLORA_STAGE_NO_EXPAND);
@@ -1312,17 +1362,18 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   if (!make_out_map(&prm.mY, a.Y, a.M, a.d_out)) return MLORA_ERR_UNSUPPORTED;
   if (a.pair_fwd) {
     prm.n_items = prm.n_tiles_rng * prm.n_nblk;
-    return launch2<FWD_MAIN>(prm, st, a.max_ctas);
+    return launch2<FWD_MAIN>(prm, st, a.max_ctas, after_shrink);
   }
   prm.n_items = 2 * prm.n_tiles_rng * prm.n_nblk;
   set_ring(prm, kA1Bytes, 4 * kBox64);
-  return launch1<FWD_MAIN>(prm, st, a.max_ctas);
+  return launch1<FWD_MAIN>(prm, st, a.max_ctas, after_shrink);
 }
 
 int tc_backward(const TcCall& a, cudaStream_t st) {
   const int n_chunks = a.plan.n_chunks;
   const int64_t zrows = int64_t(n_chunks) * kTileRows;
   int s;
+  bool after_shrink = false;  // the shrink was launched just before: the dX mainloop may overlap its tail
   if (n_chunks > 0 && (a.bwd_stages & MLORA_BWD_DZ) && a.t1 > a.t0) {
     const std::vector<ShrinkItem>& sh = a.host->shrink;
     auto lo = std::lower_bound(sh.begin(), sh.end(), a.t0, [](const ShrinkItem& v, int t) { return v.tile < t; });
@@ -1336,6 +1387,7 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     set_ring(prm, kA1Bytes, max_nc(lo, hi) * kBox64);
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dzt);
     if ((s = launch1<SHRINK_BWD>(prm, st, a.max_ctas)) != MLORA_OK) return s;
+    after_shrink = prm.n_items > 0;
   }
   if (a.dX && (a.bwd_stages & MLORA_BWD_DX)) {
     TcParams prm = base_params(a);
@@ -1354,11 +1406,11 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     if (!make_out_map(&prm.mY, a.dX, a.M, a.d_in)) return MLORA_ERR_UNSUPPORTED;
     if (a.pair_dx) {
       prm.n_items = a.plan.n_tiles * prm.n_nblk;
-      s = launch2<DX_MAIN>(prm, st, a.max_ctas);
+      s = launch2<DX_MAIN>(prm, st, a.max_ctas, after_shrink);
     } else {
       prm.n_items = 2 * a.plan.n_tiles * prm.n_nblk;
       set_ring(prm, kA1Bytes, 4 * kBox64);
-      s = launch1<DX_MAIN>(prm, st, a.max_ctas);
+      s = launch1<DX_MAIN>(prm, st, a.max_ctas, after_shrink);
     }
     if (s != MLORA_OK) return s;
   }
