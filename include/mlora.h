@@ -149,6 +149,72 @@ int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
 /* Number of plan tiles of a problem (ceil(rows / MLORA_TILE_ROWS)). */
 int32_t mlora_num_tiles(int64_t rows);
 
+/* ---- Partial-Y all-reduce of the K-sharded forward, issued from the
+ * forward's epilogue over peer memory (replaces the SUM all-reduce of each
+ * nano-batch's Y rows, phase6_two_gpu_overlap.py:247-280).
+ *
+ * Every rank of a K-sharded layer computes a partial Y over its d_in columns;
+ * Y is their sum.  Plan tile t (MLORA_TILE_ROWS rows) is owned by rank
+ * t % world.  mlora_forward_push runs the MAIN stage with an epilogue that
+ * writes each partial tile, in 256x256 blocks, into its owner's receive
+ * buffer (slot `rank`) with plain stores — to another GPU over NVLink through
+ * a peer mapping — and then adds one to the owner's arrival counter of that
+ * tile (8 arrivals per 256-column block and rank).  mlora_ar_finish has the
+ * owner wait (bounded) until all `world` partials of each of its tiles in a
+ * range have arrived, add them in rank order in fp32, and write the rounded
+ * sum into the same rows of every rank's Y, adding one per 8-row group (32 per
+ * tile) to every rank's completion counter.  mlora_ar_wait waits (bounded)
+ * until the completion counter of this rank reaches 32 n_tiles, i.e. until
+ * every row of its Y holds the sum.  A wait that runs out sets bit 1 of the error word and skips the
+ * tile (or returns).
+ *
+ * Per call sequence on each rank (counters zeroed by mlora_ar_reset, and all
+ * ranks past their reset, e.g. through a one-element collective, before any
+ * rank pushes): mlora_forward_push of each nano-batch's tile range;
+ * mlora_ar_finish of the same range (on any stream ordered after the push);
+ * mlora_ar_wait before Y is read.  Buffers are reused by the next call only
+ * after every rank's mlora_ar_wait of this one.
+ * Requires the tensor-core path (16-bit dtypes), d_out % 8 == 0, routing
+ * without out_rows, world <= MLORA_AR_MAX_RANKS. */
+#define MLORA_AR_MAX_RANKS 8
+typedef struct mlora_peer_ar {
+  int32_t rank, world;
+  int32_t n_tiles;                       /* plan tiles of the whole layer input (mlora_num_tiles) */
+  int32_t d_out;                         /* columns of Y */
+  void* recv[MLORA_AR_MAX_RANKS];        /* rank r's receive buffer, as mapped in this process */
+  uint32_t* arrive[MLORA_AR_MAX_RANKS];  /* rank r's arrival counters (mlora_ar_layout) */
+  void* y[MLORA_AR_MAX_RANKS];           /* rank r's Y [rows, d_out] */
+  uint32_t* done[MLORA_AR_MAX_RANKS];    /* rank r's completion counter */
+  int64_t timeout_ns;                    /* bound of each device-side wait; 0 = 2 s */
+} mlora_peer_ar;
+
+/* Bytes of one rank's receive buffer and of its counters (arrival counters
+ * followed by the completion counter, zeroed by mlora_ar_reset). */
+int mlora_ar_layout(int32_t n_tiles, int32_t d_out, int32_t world, size_t* recv_bytes,
+                    size_t* counter_bytes);
+/* Zero this rank's counters (ar->arrive[ar->rank], ar->done[ar->rank]). */
+int mlora_ar_reset(const mlora_peer_ar* ar, void* stream);
+/* mlora_forward_staged(stages) with MLORA_STAGE_MAIN pushing the partial
+ * tiles of [tile_begin, tile_end) to their owners instead of writing Y. */
+int mlora_forward_push(const mlora_problem* prob, const mlora_routing* route,
+                       const void* X, const void* W, const void* bias,
+                       const void* A_pack, const void* B_pack, void* zsave,
+                       void* workspace, size_t workspace_bytes, int32_t stages,
+                       int32_t tile_begin, int32_t tile_end, const mlora_peer_ar* ar, void* stream);
+/* Owner side for this rank's tiles in [tile_begin, tile_end). */
+int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dtype, int32_t tile_begin,
+                    int32_t tile_end, void* stream);
+/* Wait until every tile of this rank's Y holds the sum. */
+int mlora_ar_wait(const mlora_peer_ar* ar, void* stream);
+
+/* Peer memory for the buffers above: one cudaMalloc'd block per rank, shared
+ * with the other processes by CUDA IPC (64-byte handles). */
+int mlora_peer_alloc(size_t bytes, void** ptr);
+int mlora_peer_free(void* ptr);
+int mlora_ipc_handle(void* ptr, void* handle64);
+int mlora_ipc_open(const void* handle64, void** ptr);
+int mlora_ipc_close(void* ptr);
+
 /* Fused forward for callers that cannot allocate device memory (no
  * counterpart in the reference, which always allocates through PyTorch).
  * Serving runtimes and plugin hosts that reserve all device memory up front,

@@ -1,0 +1,307 @@
+// Owner side of the K-sharded forward's partial-Y all-reduce over peer memory
+// (mlora_ar_*, mlora_peer_* / mlora_ipc_*).
+//
+// The forward mainloop's epilogue (tc.cu, ar_push_box / ar_arrive) writes
+// every partial tile into the receive buffer of the tile's owner (rank
+// t % world) and counts it in the owner's arrival counter.  Here each owner
+// waits for the `world` partials of its tiles, adds them in rank order in
+// fp32, and writes the rounded sum into the same rows of every rank's Y with
+// plain stores through peer mappings, counting each finished 8-row group in
+// every rank's completion counter.  This is the reference's per-nano-batch SUM
+// all-reduce of the output rows (phase6_two_gpu_overlap.py:247-280) as one
+// reduce-scatter issued from the GEMM epilogue plus an owner-side gather; no
+// TMA and no multicast are involved.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace mlora {
+namespace {
+
+constexpr int kArThreads = 256;
+constexpr int kArBlock = 1 << 17;          // receive block: 256 x 256 16-bit values
+constexpr int kArSlice = 256 * 64;         // one 32-column slice of a block: 256 rows x 64 bytes
+constexpr int kArRows = 8;                          // rows of one finisher work unit (one warp)
+constexpr int kArGroupsPerTile = kTileRows / kArRows;  // units per tile
+constexpr unsigned long long kArDefaultTimeoutNs = 2000000000ull;
+
+struct ArFinish {
+  int rank, world, lt_stride, n_nblk, d_out;
+  int t_first, n_owned;  // first tile of the range this rank owns; owned tiles in the range
+  int f16;
+  int64_t M;
+  unsigned arrive_target;  // world * 8 * n_nblk
+  unsigned long long timeout_ns;
+  const uint8_t* recv;
+  const unsigned* arrive;
+  uint8_t* y[MLORA_AR_MAX_RANKS];
+  unsigned* done[MLORA_AR_MAX_RANKS];
+};
+
+struct ArWait {
+  const unsigned* done;
+  unsigned target;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ar_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Whole warp: wait until *c >= target (every lane reads the counter with
+// acquire semantics), at most timeout_ns.  Returns false on timeout.
+__device__ bool ar_wait_count(const unsigned* c, unsigned target, unsigned long long timeout_ns) {
+  const unsigned long long t0 = ar_now();
+  unsigned nap = 64;
+  for (;;) {
+    const bool ready = ld_acquire_sys(c) >= target;
+    if (__all_sync(0xffffffffu, ready)) return true;
+    const bool late = __shfl_sync(0xffffffffu, ar_now() - t0 > timeout_ns ? 1 : 0, 0) != 0;
+    if (late) return false;
+    __nanosleep(nap);
+    if (nap < 2048) nap *= 2;
+  }
+}
+
+__device__ __forceinline__ void add8(float* acc, const uint4 v, int f16) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float2 h;
+    if (f16) {
+      h = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+    } else {
+      h = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+    }
+    acc[2 * e] += h.x;
+    acc[2 * e + 1] += h.y;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_pair(float a, float b, int f16) {
+  if (f16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// One warp per (owned tile, 8-row group); lane l covers columns
+// 32 (l / 4) + 8 (l % 4) .. +8 of every 256-column block, so that a warp
+// reads 512 contiguous bytes of each slot and writes 512 contiguous bytes of
+// each Y row per block.  PMAX (1, 2, 4 or 8) bounds the ranks; BU blocks are
+// loaded together so that 8 16-byte loads per lane are in flight.
+template <int PMAX>
+__global__ void __launch_bounds__(kArThreads) k_ar_finish(const __grid_constant__ ArFinish a) {
+  constexpr int BU = PMAX >= 8 ? 1 : (PMAX >= 4 ? 2 : 4);
+  const int lane = threadIdx.x & 31;
+  const int gw = int((blockIdx.x * kArThreads + threadIdx.x) >> 5);
+  const int nw = int((gridDim.x * kArThreads) >> 5);
+  const int units = a.n_owned * kArGroupsPerTile;
+  const int s = lane >> 2, c = lane & 3;
+  const size_t slot_stride = size_t(a.lt_stride) * size_t(a.n_nblk) * kArBlock;
+  for (int u = gw; u < units; u += nw) {
+    const int tile = a.t_first + (u / kArGroupsPerTile) * a.world;
+    const int rg = u % kArGroupsPerTile;
+    const int lt = tile / a.world;
+    if (lt >= a.lt_stride) {  // cannot happen for a range inside the layout
+      if (lane == 0) atomicOr(&g_err_word, kErrBounds);
+      continue;
+    }
+    if (!ar_wait_count(a.arrive + lt, a.arrive_target, a.timeout_ns)) {
+      // no completion count for this group: every rank waiting for it times out too
+      if (lane == 0) atomicOr(&g_err_word, kErrTimeout);
+      continue;
+    }
+    const uint8_t* base = a.recv + size_t(lt) * size_t(a.n_nblk) * kArBlock + s * kArSlice + c * 16;
+    for (int j = 0; j < kArRows; ++j) {
+      const int r = rg * kArRows + j;
+      const int64_t row = int64_t(tile) * kTileRows + r;
+      if (row >= a.M) break;
+      for (int b0 = 0; b0 < a.n_nblk; b0 += BU) {
+        uint4 v[BU][PMAX];
+#pragma unroll
+        for (int q = 0; q < BU; ++q) {
+          const int col = (b0 + q) * 256 + s * 32 + c * 8;
+          if (b0 + q < a.n_nblk && col < a.d_out) {  // d_out % 8 == 0: an 8-column chunk is whole or absent
+            const uint8_t* src = base + size_t(b0 + q) * kArBlock + r * 64;
+#pragma unroll
+            for (int p = 0; p < PMAX; ++p)
+              if (p < a.world) v[q][p] = *reinterpret_cast<const uint4*>(src + p * slot_stride);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < BU; ++q) {
+          const int col = (b0 + q) * 256 + s * 32 + c * 8;
+          if (b0 + q >= a.n_nblk || col >= a.d_out) continue;
+          float acc[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+          for (int p = 0; p < PMAX; ++p)
+            if (p < a.world) add8(acc, v[q][p], a.f16);
+          const uint4 o = make_uint4(pack_pair(acc[0], acc[1], a.f16), pack_pair(acc[2], acc[3], a.f16),
+                                     pack_pair(acc[4], acc[5], a.f16), pack_pair(acc[6], acc[7], a.f16));
+          const size_t off = (size_t(row) * a.d_out + col) * 2;
+#pragma unroll
+          for (int d = 0; d < PMAX; ++d)
+            if (d < a.world) *reinterpret_cast<uint4*>(a.y[d] + off) = o;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int d = 0; d < a.world; ++d)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.done[d]) : "memory");
+    }
+  }
+}
+
+__global__ void k_ar_wait(const __grid_constant__ ArWait w) {
+  if (!ar_wait_count(w.done, w.target, w.timeout_ns) && threadIdx.x == 0) atomicOr(&g_err_word, kErrTimeout);
+}
+
+int lt_stride_of(int n_tiles, int world) { return (n_tiles + world - 1) / world; }
+
+// Checks shared by every entry point.
+int check_ar(const mlora_peer_ar* ar) {
+  if (!ar) return MLORA_ERR_INVALID_ARG;
+  if (ar->world < 1 || ar->world > MLORA_AR_MAX_RANKS || ar->rank < 0 || ar->rank >= ar->world)
+    return MLORA_ERR_INVALID_ARG;
+  if (ar->n_tiles < 1 || ar->d_out < 8 || ar->d_out % 8 != 0 || ar->timeout_ns < 0) return MLORA_ERR_INVALID_ARG;
+  for (int r = 0; r < ar->world; ++r)
+    if (!ar->recv[r] || !ar->arrive[r] || !ar->y[r] || !ar->done[r]) return MLORA_ERR_INVALID_ARG;
+  return MLORA_OK;
+}
+
+unsigned long long timeout_of(const mlora_peer_ar* ar) {
+  return ar->timeout_ns > 0 ? static_cast<unsigned long long>(ar->timeout_ns) : kArDefaultTimeoutNs;
+}
+
+}  // namespace
+}  // namespace mlora
+
+using namespace mlora;
+
+extern "C" int mlora_ar_layout(int32_t n_tiles, int32_t d_out, int32_t world, size_t* recv_bytes,
+                               size_t* counter_bytes) {
+  if (n_tiles < 1 || d_out < 8 || d_out % 8 != 0 || world < 1 || world > MLORA_AR_MAX_RANKS || !recv_bytes ||
+      !counter_bytes)
+    return MLORA_ERR_INVALID_ARG;
+  const size_t lt = size_t(lt_stride_of(n_tiles, world));
+  const size_t nblk = size_t((d_out + 255) / 256);
+  *recv_bytes = size_t(world) * lt * nblk * kArBlock;
+  *counter_bytes = ((lt + 1) * sizeof(uint32_t) + 255) / 256 * 256;
+  return MLORA_OK;
+}
+
+extern "C" int mlora_ar_reset(const mlora_peer_ar* ar, void* stream) {
+  int st = check_ar(ar);
+  if (st != MLORA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t lt = size_t(lt_stride_of(ar->n_tiles, ar->world));
+  MLORA_CUDA_TRY(cudaMemsetAsync(ar->arrive[ar->rank], 0, lt * sizeof(uint32_t), s));
+  MLORA_CUDA_TRY(cudaMemsetAsync(ar->done[ar->rank], 0, sizeof(uint32_t), s));
+  return MLORA_OK;
+}
+
+extern "C" int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dtype, int32_t tile_begin,
+                               int32_t tile_end, void* stream) {
+  int st = check_ar(ar);
+  if (st != MLORA_OK) return st;
+  if (dtype != MLORA_BF16 && dtype != MLORA_F16) return MLORA_ERR_UNSUPPORTED;
+  if (rows < 1 || mlora_num_tiles(rows) != ar->n_tiles) return MLORA_ERR_INVALID_ARG;
+  if (tile_begin < 0 || tile_end < tile_begin || tile_end > ar->n_tiles) return MLORA_ERR_INVALID_ARG;
+  ArFinish a = {};
+  a.rank = ar->rank;
+  a.world = ar->world;
+  a.lt_stride = lt_stride_of(ar->n_tiles, ar->world);
+  a.n_nblk = (ar->d_out + 255) / 256;
+  a.d_out = ar->d_out;
+  a.f16 = dtype == MLORA_F16 ? 1 : 0;
+  a.M = rows;
+  // first tile t >= tile_begin with t % world == rank
+  a.t_first = tile_begin + ((ar->rank - tile_begin % ar->world) + ar->world) % ar->world;
+  a.n_owned = a.t_first < tile_end ? (tile_end - 1 - a.t_first) / ar->world + 1 : 0;
+  if (a.n_owned == 0) return MLORA_OK;
+  a.arrive_target = unsigned(ar->world) * 8u * unsigned(a.n_nblk);
+  a.timeout_ns = timeout_of(ar);
+  a.recv = static_cast<const uint8_t*>(ar->recv[ar->rank]);
+  a.arrive = ar->arrive[ar->rank];
+  for (int r = 0; r < ar->world; ++r) {
+    a.y[r] = static_cast<uint8_t*>(ar->y[r]);
+    a.done[r] = ar->done[r];
+  }
+  int dev = 0, sms = 0;
+  MLORA_CUDA_TRY(cudaGetDevice(&dev));
+  MLORA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int warps = a.n_owned * kArGroupsPerTile;
+  int grid = (warps + kArThreads / 32 - 1) / (kArThreads / 32);
+  if (grid > sms) grid = sms;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a.world == 1) k_ar_finish<1><<<grid, kArThreads, 0, s>>>(a);
+  else if (a.world == 2) k_ar_finish<2><<<grid, kArThreads, 0, s>>>(a);
+  else if (a.world <= 4) k_ar_finish<4><<<grid, kArThreads, 0, s>>>(a);
+  else k_ar_finish<8><<<grid, kArThreads, 0, s>>>(a);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
+  int st = check_ar(ar);
+  if (st != MLORA_OK) return st;
+  ArWait w;
+  w.done = ar->done[ar->rank];
+  w.target = unsigned(kArGroupsPerTile) * unsigned(ar->n_tiles);
+  w.timeout_ns = timeout_of(ar);
+  k_ar_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+extern "C" int mlora_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return MLORA_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  MLORA_CUDA_TRY(cudaMalloc(ptr, bytes));
+  return MLORA_OK;
+}
+
+extern "C" int mlora_peer_free(void* ptr) {
+  if (!ptr) return MLORA_OK;
+  MLORA_CUDA_TRY(cudaFree(ptr));
+  return MLORA_OK;
+}
+
+extern "C" int mlora_ipc_handle(void* ptr, void* handle64) {
+  if (!ptr || !handle64) return MLORA_ERR_INVALID_ARG;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  cudaIpcMemHandle_t h;
+  MLORA_CUDA_TRY(cudaIpcGetMemHandle(&h, ptr));
+  memcpy(handle64, &h, sizeof(h));
+  return MLORA_OK;
+}
+
+extern "C" int mlora_ipc_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) return MLORA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  *ptr = nullptr;
+  MLORA_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MLORA_OK;
+}
+
+extern "C" int mlora_ipc_close(void* ptr) {
+  if (!ptr) return MLORA_ERR_INVALID_ARG;
+  MLORA_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return MLORA_OK;
+}

@@ -126,11 +126,14 @@ extern "C" int32_t mlora_num_tiles(int64_t rows) {
   return rows <= 0 ? 0 : int32_t((rows + kTileRows - 1) / kTileRows);
 }
 
-extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
-                                    const void* X, const void* W, const void* bias,
-                                    const void* A_pack, const void* B_pack, void* Y, void* zsave,
-                                    void* workspace, size_t workspace_bytes, int32_t stages,
-                                    int32_t tile_begin, int32_t tile_end, void* stream) {
+namespace {
+
+// mlora_forward_staged, or with `ar` mlora_forward_push (MAIN pushes the
+// partial tiles to their owner ranks instead of writing Y).
+int forward_staged(const mlora_problem* prob, const mlora_routing* route, const void* X, const void* W,
+                   const void* bias, const void* A_pack, const void* B_pack, void* Y, void* zsave,
+                   void* workspace, size_t workspace_bytes, int32_t stages, int32_t tile_begin,
+                   int32_t tile_end, const mlora_peer_ar* ar, void* stream) {
   thread_local Plan p;
   int st = build_plan(prob, route, &p);
   if (st != MLORA_OK) return st;
@@ -140,7 +143,7 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
   const bool need_z = !p.chunks.empty() &&
                       ((stages & MLORA_STAGE_SHRINK) || ((stages & MLORA_STAGE_MAIN) && !(stages & MLORA_STAGE_NO_EXPAND)));
   if (!X || !workspace) return MLORA_ERR_INVALID_ARG;
-  if ((stages & MLORA_STAGE_MAIN) && !Y) return MLORA_ERR_INVALID_ARG;
+  if ((stages & MLORA_STAGE_MAIN) && !Y && !ar) return MLORA_ERR_INVALID_ARG;
   if (need_z && !zsave) return MLORA_ERR_INVALID_ARG;
   if (!p.chunks.empty() && (stages & MLORA_STAGE_SHRINK) && !A_pack) return MLORA_ERR_INVALID_ARG;
   if (need_z && (stages & MLORA_STAGE_MAIN) && !(stages & MLORA_STAGE_NO_EXPAND) && !B_pack)
@@ -148,12 +151,14 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
   const int impl = choose_impl(prob);
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
+  if (ar && (impl != MLORA_IMPL_TC || route->out_rows)) return MLORA_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
   PlanDev dev;
   st = stage_plan(prob, p, workspace, s, &dev);
   if (st != MLORA_OK) return st;
   if (impl == MLORA_IMPL_TC) {
     TcCall a;
+    a.ar = ar;
     a.plan = dev;
     a.host = &p;
     a.M = prob->rows; a.d_in = prob->d_in; a.d_out = prob->d_out; a.R = route->r_pack;
@@ -177,6 +182,34 @@ extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routi
   a.c_begin = p.tile_chunk_begin[tile_begin];
   a.c_end = p.tile_chunk_begin[tile_end];
   return simt_forward(a, s);
+}
+
+}  // namespace
+
+extern "C" int mlora_forward_staged(const mlora_problem* prob, const mlora_routing* route,
+                                    const void* X, const void* W, const void* bias,
+                                    const void* A_pack, const void* B_pack, void* Y, void* zsave,
+                                    void* workspace, size_t workspace_bytes, int32_t stages,
+                                    int32_t tile_begin, int32_t tile_end, void* stream) {
+  return forward_staged(prob, route, X, W, bias, A_pack, B_pack, Y, zsave, workspace, workspace_bytes, stages,
+                        tile_begin, tile_end, nullptr, stream);
+}
+
+extern "C" int mlora_forward_push(const mlora_problem* prob, const mlora_routing* route,
+                                  const void* X, const void* W, const void* bias,
+                                  const void* A_pack, const void* B_pack, void* zsave,
+                                  void* workspace, size_t workspace_bytes, int32_t stages,
+                                  int32_t tile_begin, int32_t tile_end, const mlora_peer_ar* ar, void* stream) {
+  if (!prob || !route || !ar) return MLORA_ERR_INVALID_ARG;
+  if (ar->world < 1 || ar->world > MLORA_AR_MAX_RANKS || ar->rank < 0 || ar->rank >= ar->world)
+    return MLORA_ERR_INVALID_ARG;
+  if (ar->d_out != prob->d_out || ar->d_out % 8 != 0 || ar->n_tiles != mlora_num_tiles(prob->rows))
+    return MLORA_ERR_INVALID_ARG;
+  for (int r = 0; r < ar->world; ++r)
+    if (!ar->recv[r] || !ar->arrive[r]) return MLORA_ERR_INVALID_ARG;
+  if (prob->dtype != MLORA_BF16 && prob->dtype != MLORA_F16) return MLORA_ERR_UNSUPPORTED;
+  return forward_staged(prob, route, X, W, bias, A_pack, B_pack, nullptr, zsave, workspace, workspace_bytes,
+                        stages, tile_begin, tile_end, ar, stream);
 }
 
 extern "C" int mlora_forward(const mlora_problem* prob, const mlora_routing* route, const void* X,

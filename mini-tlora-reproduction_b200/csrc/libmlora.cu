@@ -6,5 +6,6 @@
 #include "simt.cu"
 #include "route.cu"
 #include "tc.cu"
+#include "allreduce.cu"
 #include "api.cu"
 #include "noalloc.cu"

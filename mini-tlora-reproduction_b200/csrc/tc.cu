@@ -117,6 +117,11 @@ struct TcParams {
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
   __nv_bfloat16* dA;
   __nv_bfloat16* dB;
+  // forward main with the peer all-reduce: partial tiles go to their owner
+  // rank's receive buffer (slot ar_rank) instead of Y
+  int ar_on, ar_rank, ar_world, ar_lt_stride;
+  uint8_t* ar_recv[MLORA_AR_MAX_RANKS];
+  unsigned* ar_arrive[MLORA_AR_MAX_RANKS];
 };
 
 // ------------------------------------------------------------------ PTX
@@ -271,6 +276,11 @@ __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk
 __device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -534,6 +544,55 @@ __device__ __forceinline__ bool sched_take(SchedQ& s, bool remote, volatile int*
 // lane.  With NBUF = 2, `buf` alternates between the warp's two buffers; the
 // store issued from the same buffer NBUF slices earlier must have finished
 // reading it.
+// Receive-buffer block of the peer all-reduce: (slot, owned tile, 256-column
+// block) = 256 x 256 16-bit values stored as 8 column slices of 32, each
+// 256 rows x 64 bytes, so that an epilogue warp's 32x32 box is 2 KB of
+// contiguous memory.
+constexpr int kArBlockShift = 17;  // 128 KB per block
+constexpr int kArSliceBytes = 256 * 64;
+
+// One warp's 32x32 box of the partial Y (rows row_w0.., columns n0 + col..)
+// to its owner: staged in shared memory (64-byte swizzle, as for the TMA
+// store), then written as four fully coalesced 512-byte rows of lanes.
+__device__ __forceinline__ void ar_push_box(const TcParams& p, int64_t row_w0, int n0, int col, const float* f,
+                                            uint32_t buf, int lane) {
+  __syncwarp();  // the previous box's reads of this buffer are done
+  const uint32_t rowb = buf + uint32_t(lane) * 64u;
+  const uint32_t sw = uint32_t(lane >> 1) & 3u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    sts128(rowb + ((uint32_t(q) ^ sw) << 4), pack2(f[8 * q], f[8 * q + 1], p.f16),
+           pack2(f[8 * q + 2], f[8 * q + 3], p.f16), pack2(f[8 * q + 4], f[8 * q + 5], p.f16),
+           pack2(f[8 * q + 6], f[8 * q + 7], p.f16));
+  __syncwarp();
+  const int64_t tile = row_w0 >> 8;
+  const int owner = int(tile % p.ar_world);
+  const int64_t lt = tile / p.ar_world;
+  uint8_t* dst = p.ar_recv[owner] +
+                 (((int64_t(p.ar_rank) * p.ar_lt_stride + lt) * p.n_nblk + (n0 >> 8)) << kArBlockShift) +
+                 (col >> 5) * kArSliceBytes + (row_w0 & 255) * 64;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t R = uint32_t(8 * q + (lane >> 2));  // box row of this lane's 16 bytes
+    const uint32_t c = uint32_t(lane & 3);
+    const uint4 v = lds128(buf + R * 64u + ((c ^ ((R >> 1) & 3u)) << 4));
+    *reinterpret_cast<uint4*>(dst + q * 512 + lane * 16) = v;
+  }
+}
+
+// After all boxes of an item: count the warp's 32 rows x 256 columns in the
+// owner's arrival counter of the tile (release at system scope, so the owner
+// that sees the count also sees the boxes).
+__device__ __forceinline__ void ar_arrive(const TcParams& p, int tile, int lane) {
+  __syncwarp();
+  if (lane == 0) {
+    const int owner = tile % p.ar_world;
+    unsigned* c = p.ar_arrive[owner] + tile / p.ar_world;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
+  }
+}
+
 template <int MODE, int NBUF>
 __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0, int n0, int col, bool empty_acc,
                                                uint32_t taddr, uint32_t buf, int lane) {
@@ -567,6 +626,10 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
       for (int q = 0; q < 32; ++q)
         if (n0 + col + q < N) f[q] += ld1(p.bias + n0 + col + q, p.f16);
     }
+  }
+  if (MODE == FWD_MAIN && p.ar_on) {
+    ar_push_box(p, row_w0, n0, col, f, buf, lane);
+    return;
   }
   if (p.out_rows) {
     // rows sorted by adapter: each lane writes its row's 32 values straight to
@@ -889,6 +952,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+      if (MODE == FWD_MAIN && p.ar_on) ar_arrive(p, it.t, lane);
     }
     if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
@@ -1114,6 +1178,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);  // one remote arrival per warp
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+      if (MODE == FWD_MAIN && p.ar_on) ar_arrive(p, it.t, lane);
     }
     if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
@@ -1359,7 +1424,20 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
   prm.out_rows = a.out_rows;
-  if (!make_out_map(&prm.mY, a.Y, a.M, a.d_out)) return MLORA_ERR_UNSUPPORTED;
+  if (a.ar) {
+    // partial tiles go to their owners' receive buffers (layout of mlora_ar_layout)
+    if (a.out_rows || a.ar->n_tiles != a.plan.n_tiles || a.ar->d_out != a.d_out) return MLORA_ERR_INVALID_ARG;
+    prm.ar_on = 1;
+    prm.ar_rank = a.ar->rank;
+    prm.ar_world = a.ar->world;
+    prm.ar_lt_stride = (a.ar->n_tiles + a.ar->world - 1) / a.ar->world;
+    for (int r = 0; r < a.ar->world; ++r) {
+      prm.ar_recv[r] = static_cast<uint8_t*>(a.ar->recv[r]);
+      prm.ar_arrive[r] = a.ar->arrive[r];
+    }
+  } else if (!make_out_map(&prm.mY, a.Y, a.M, a.d_out)) {
+    return MLORA_ERR_UNSUPPORTED;
+  }
   if (a.pair_fwd) {
     prm.n_items = prm.n_tiles_rng * prm.n_nblk;
     return launch2<FWD_MAIN>(prm, st, a.max_ctas, after_shrink);

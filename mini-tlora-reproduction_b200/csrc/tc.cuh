@@ -28,6 +28,8 @@ struct TcCall {
   int db0 = 0, db1 = 0;
   bool pair_fwd = false;  // forward mainloop on 2-SM pairs (tcgen05 cta_group::2)
   bool pair_dx = true;    // dX mainloop on 2-SM pairs
+  // forward MAIN: push the partial tiles to their owner ranks (mlora_forward_push)
+  const mlora_peer_ar* ar = nullptr;
 };
 
 // true when the driver exposes cuTensorMapEncodeTiled and the current device

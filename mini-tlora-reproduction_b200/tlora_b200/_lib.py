@@ -78,6 +78,24 @@ class Routing(ctypes.Structure):
     ]
 
 
+AR_MAX_RANKS = 8
+
+
+class PeerAr(ctypes.Structure):
+    """mlora_peer_ar: the peer buffers of the K-sharded forward's all-reduce."""
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("n_tiles", ctypes.c_int32),
+        ("d_out", ctypes.c_int32),
+        ("recv", ctypes.c_void_p * AR_MAX_RANKS),
+        ("arrive", ctypes.c_void_p * AR_MAX_RANKS),
+        ("y", ctypes.c_void_p * AR_MAX_RANKS),
+        ("done", ctypes.c_void_p * AR_MAX_RANKS),
+        ("timeout_ns", ctypes.c_int64),
+    ]
+
+
 class SgdItem(ctypes.Structure):
     _fields_ = [
         ("param", ctypes.c_void_p),
@@ -101,6 +119,20 @@ SIGNATURES = {
                                             _VP, _VP, _VP, _VP, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, _VP]),
     "mlora_num_tiles": (ctypes.c_int32, [ctypes.c_int64]),
+    "mlora_ar_layout": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
+    "mlora_ar_reset": (ctypes.c_int, [ctypes.POINTER(PeerAr), _VP]),
+    "mlora_forward_push": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,
+                                          _VP, _VP, _VP, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.POINTER(PeerAr), _VP]),
+    "mlora_ar_finish": (ctypes.c_int, [ctypes.POINTER(PeerAr), ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_int32, _VP]),
+    "mlora_ar_wait": (ctypes.c_int, [ctypes.POINTER(PeerAr), _VP]),
+    "mlora_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "mlora_peer_free": (ctypes.c_int, [_VP]),
+    "mlora_ipc_handle": (ctypes.c_int, [_VP, _VP]),
+    "mlora_ipc_open": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
+    "mlora_ipc_close": (ctypes.c_int, [_VP]),
     "mlora_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP,
                                              _VP, _VP, _VP]),
     "mlora_backward": (ctypes.c_int, [ctypes.POINTER(Problem), ctypes.POINTER(Routing), _VP, _VP, _VP, _VP, _VP,

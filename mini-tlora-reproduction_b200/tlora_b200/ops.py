@@ -336,6 +336,17 @@ class StagedForward:
         finally:
             self.args.prob.max_ctas = old
 
+    def push(self, ar, t0=0, t1=None, expand=True, add_bias=True):
+        """``main`` whose epilogue writes the partial tiles of [t0, t1) into
+        their owner ranks' receive buffers (``ar``: a peer.PeerAllReduce of
+        this layer's rows) instead of ``y``; the owners' ``ar.finish`` adds
+        them up (mlora_forward_push)."""
+        stages = _lib.STAGE_MAIN | (0 if expand else _lib.STAGE_NO_EXPAND)
+        _lib.call("mlora_forward_push", ctypes.byref(self.args.prob), ctypes.byref(self.args.route),
+                  _ptr(self.x), _ptr(self.W), _ptr(self.bias if add_bias else None), _ptr(self.st.A_pack),
+                  _ptr(self.st.B_pack), _ptr(self.z), _ptr(self.ws), self.wb, stages, t0,
+                  self.n_tiles if t1 is None else t1, ctypes.byref(ar.ar), _stream(self.x.device))
+
 
 def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, want_dB: bool):
     """Run mlora_backward; returns (dX in the caller's row order or None,

@@ -27,6 +27,14 @@ sum_p Z_p = Z.  Per step:
 
 Nano-batch boundaries are rounded to 256-row plan tiles (the reference splits rows
 exactly); N still counts nano-batches.
+
+The Y all-reduce of step 2 has two implementations (``ShardedLayer.comm``):
+"nccl" (an async SUM all-reduce per nano-batch, as the reference) and "peer"
+(peer.PeerAllReduce: the mainloop's epilogue writes each partial tile straight
+into its owner rank's receive buffer over NVLink, and a small owner kernel on
+a side stream adds the partials of its tiles and writes the sums into every
+rank's Y while the next nano-batch's mainloop runs).  The routing plan must
+keep the rows in their order (adapter-sorted ids).
 """
 
 from __future__ import annotations
@@ -40,7 +48,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import ops, peer
 from ._lib import TILE_ROWS
 from .nano import AIMDController, split_ranges
 
@@ -99,9 +107,9 @@ class NativeCompute:
             self._sms = torch.cuda.get_device_properties(device).multi_processor_count
         return max(1, self._sms - self.comm_sms)
 
-    def begin(self, layer, x_p, plan):
+    def begin(self, layer, x_p, plan, y=None):
         st = ops.LayerState(layer.table, layer.scaling, plan, layer.A_pack, layer.B_pack, self.impl)
-        fw = ops.StagedForward(x_p, layer.W, layer.bias, st)
+        fw = ops.StagedForward(x_p, layer.W, layer.bias, st, y=y)
         zbytes = ops._CallArgs(x_p.shape[0], x_p.shape[1], layer.B_pack.shape[0], ops.mlora_dtype(x_p.dtype),
                                self.impl, plan, layer.table, layer.scaling).sizes()[0]
         zview = fw.z[:zbytes].view(x_p.dtype) if zbytes else None
@@ -112,6 +120,9 @@ class NativeCompute:
 
     def main(self, ctx, t0, t1, expand, add_bias):
         ctx["fw"].main(t0, t1, expand=expand, add_bias=add_bias, max_ctas=self._main_ctas(ctx["fw"].x.device))
+
+    def push(self, ctx, ar, t0, t1, expand, add_bias):
+        ctx["fw"].push(ar, t0, t1, expand=expand, add_bias=add_bias)
 
     def bwd_begin(self, ctx, layer, x_p, dy, overlapped=False):
         st = ctx["st"]
@@ -146,11 +157,17 @@ class NativeCompute:
 class ShardedLayer:
     """Rank ``rank``'s K-shard of a MultiLoRALinear (see module docstring)."""
 
-    def __init__(self, model, rank: int, world: int, compute=None, group=None, bwd_group=None):
+    def __init__(self, model, rank: int, world: int, compute=None, group=None, bwd_group=None,
+                 comm: str = "nccl"):
         # `bwd_group`: a second communicator for the backward's small
         # all-reduces (dZ, dB), so they do not queue behind the large Y
         # all-reduces still in flight on `group`
+        if comm not in ("nccl", "peer"):
+            raise ValueError(f"comm must be 'nccl' or 'peer', not {comm!r}")
         self.rank, self.world, self.group = rank, world, group
+        self.comm = comm
+        self._ar = None
+        self._last_done = None
         self.bwd_group = bwd_group if bwd_group is not None else group
         A_pack, B_pack, table = model.packed()
         d_in = model.base.in_features
@@ -180,6 +197,8 @@ class ShardedLayer:
     def forward_async(self, x_p, plan, n_nano: int, pipelined: bool = True, comm: bool = True):
         """Pipelined forward that returns with the nano-batch all-reduces still
         in flight: (Y, ctx, Y work handles, Z work handle or None)."""
+        if comm and pipelined and self.comm == "peer" and self.world > 1:
+            return self._forward_peer(x_p, plan, n_nano)
         c = self.compute
         ctx = c.begin(self, x_p, plan)
         with _Range("mlora.shrink"):
@@ -204,6 +223,76 @@ class ShardedLayer:
                 else:
                     dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=self.group)
         return ctx["y"], ctx, works, hz
+
+    def peer_buffers(self, rows: int, dtype, device) -> "peer.PeerAllReduce":
+        """This rank's peer all-reduce buffers for ``rows`` rows (collective
+        on first use or when the row count changes)."""
+        if self._ar is None or self._ar.rows != rows:
+            if self._ar is not None:
+                torch.cuda.synchronize(device)
+                dist.barrier(group=self.group)  # no rank still writes into the old buffers
+                self._ar.close()
+            d_out = self.B_pack.shape[0]
+            self._ar = peer.PeerAllReduce.over_group(rows, d_out, dtype, device, self.group)
+            self._one = torch.zeros(1, dtype=torch.float32, device=device)
+            self._side = torch.cuda.Stream(device)
+        return self._ar
+
+    def _forward_peer(self, x_p, plan, n_nano: int):
+        """forward_async with the Y all-reduce issued from the forward epilogue
+        (peer.PeerAllReduce); the returned work handle makes the caller's
+        stream wait until every row of Y holds the sum.  Y is the peer buffer
+        and is overwritten by this layer's next forward."""
+        if plan.perm is not None:
+            raise ValueError("the peer all-reduce needs a routing plan that keeps the row order")
+        c = self.compute
+        dev = x_p.device
+        rows = x_p.shape[0]
+        ar = self.peer_buffers(rows, x_p.dtype, dev)
+        cur = torch.cuda.current_stream(dev)
+        if self._last_done is not None:
+            cur.wait_event(self._last_done)  # this rank's previous call is finished with the buffers
+        ar.reset(cur)
+        # every rank's counters are zero before any rank pushes (and every
+        # rank's previous call has finished with the buffers)
+        dist.all_reduce(self._one, op=dist.ReduceOp.SUM, group=self.group)
+        ctx = c.begin(self, x_p, plan, y=ar.y)
+        with _Range("mlora.shrink"):
+            c.shrink(ctx)
+        hz = None
+        if ctx["z"] is not None:
+            hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        owner = self.rank == 0
+        if owner and hz is not None:
+            hz.wait()
+            hz = None
+        side = self._side
+        for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
+            with _Range(f"mlora.nano{i}"):
+                c.push(ctx, ar, t0, t1, expand=owner, add_bias=owner)
+                ev = torch.cuda.Event()
+                ev.record(cur)
+                side.wait_event(ev)
+                ar.finish(t0, t1, side)
+        ar.wait(side)
+        done = torch.cuda.Event()
+        done.record(side)
+        self._last_done = done
+        return ar.y, ctx, [_EventWork(done, dev)], hz
+
+    def close(self) -> None:
+        """Release the peer buffers (collective: every rank calls it after its
+        device work; each rank unmaps its peers' buffers before any rank frees
+        its own)."""
+        if self._ar is None:
+            return
+        torch.cuda.synchronize(self._ar.device)
+        dist.barrier(group=self.group)
+        self._ar.close_peers()
+        dist.barrier(group=self.group)
+        self._ar.close()
+        self._ar = None
+        self._last_done = None
 
     def backward(self, ctx, x_p, dy, overlapped=False):
         """Backward on this rank's shard.  dZ (needs all of dY and B) and dB
@@ -239,6 +328,18 @@ class ShardedLayer:
         for w in works:
             w.wait()
         return y, dx_p
+
+
+class _EventWork:
+    """Work handle of the peer all-reduce: wait() makes the current stream
+    wait for the side stream's completion event (as an NCCL work handle's
+    wait() does for its collective)."""
+
+    def __init__(self, ev: torch.cuda.Event, device):
+        self.ev, self.device = ev, device
+
+    def wait(self):
+        torch.cuda.current_stream(self.device).wait_event(self.ev)
 
 
 def comm_only(layer: ShardedLayer, y: torch.Tensor, z: Optional[torch.Tensor], n_tiles: int, n_nano: int):
@@ -456,6 +557,28 @@ def _ksharded(args, rank, world, dev, comm_sms):
     t_comm = _timed_med(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
     hidden = 1.0 - max(0.0, t_pipe - t_compute) / t_comm if t_comm > 0 else 0.0
     ms = _timed_med(stepper(best_n), args.steps, dev)
+
+    # the same pipeline with the Y all-reduce issued from the forward epilogue
+    # over peer memory (peer.PeerAllReduce) instead of NCCL
+    peer_res = None
+    if world > 1:
+        layer.comm = "peer"
+        layer.compute.comm_sms = 0
+        for _ in range(3):
+            stepper(best_n)()
+        torch.cuda.synchronize(dev)
+        p_sweep = {n: _timed_med(stepper(n), 3, dev) for n in (1, 2, 4, 8, 16) if n <= n_tiles}
+        pn = min(p_sweep, key=p_sweep.get)
+        p_ms = _timed_med(stepper(pn), args.steps, dev)
+        err = _lib.device_error()
+        peer_res = {"n": pn, "value": round(sp.rows / (p_ms / 1000.0), 1), "ms_per_step": round(p_ms, 4),
+                    "step_tflops": round(sp.flops() / (p_ms / 1000.0) / 1e12, 1),
+                    "exposed_over_compute_ms": round(p_ms - t_compute, 4),
+                    "n_sweep_ms": {str(k): round(v, 4) for k, v in p_sweep.items()},
+                    "device_error": int(err)}
+        layer.comm = "nccl"
+        layer.compute.comm_sms = best_k
+        layer.close()
     del w
     if rank != 0:
         return None
@@ -468,4 +591,5 @@ def _ksharded(args, rank, world, dev, comm_sms):
                         "compute_only_ms": round(t_compute, 4), "comm_only_ms": round(t_comm, 4),
                         "comm_hidden_frac": round(hidden, 4)},
             "n_sweep_ms": {str(k): round(v, 4) for k, v in n_sweep.items()},
-            "aimd": horizons}
+            "aimd": horizons,
+            "peer_allreduce": peer_res}

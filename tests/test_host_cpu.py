@@ -52,6 +52,33 @@ def test_status_strings_and_sizes_without_gpu():
         ops._CallArgs(300, 256, 128, _lib.BF16, "auto", bad, table, np.ones(3, np.float32)).sizes()
 
 
+def test_peer_allreduce_layout_and_checks_without_gpu():
+    """Receive-buffer and counter sizes of the peer all-reduce (host
+    arithmetic), and the argument checks that run before any CUDA call."""
+    import ctypes
+
+    lib = _lib.lib()
+    recv, cnt = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    # c3: 40,960 rows = 160 tiles, d_out 8192 = 32 blocks of 256 columns
+    for world, lt in ((1, 160), (2, 80), (3, 54), (8, 20)):
+        assert lib.mlora_ar_layout(160, 8192, world, ctypes.byref(recv), ctypes.byref(cnt)) == 0
+        assert recv.value == world * lt * 32 * 256 * 256 * 2
+        assert cnt.value >= 4 * (lt + 1) and cnt.value % 256 == 0
+    # a partial last block still takes a whole 256-column block
+    assert lib.mlora_ar_layout(4, 1000, 2, ctypes.byref(recv), ctypes.byref(cnt)) == 0
+    assert recv.value == 2 * 2 * 4 * 256 * 256 * 2
+    for bad in ((0, 8192, 2), (4, 1004, 2), (4, 8192, 0), (4, 8192, 9)):
+        assert lib.mlora_ar_layout(*bad, ctypes.byref(recv), ctypes.byref(cnt)) == _lib.ERR_INVALID_ARG
+    ar = _lib.PeerAr()
+    ar.rank, ar.world, ar.n_tiles, ar.d_out = 0, 2, 4, 1000
+    # null peer pointers are rejected before anything is launched
+    assert lib.mlora_ar_finish(ctypes.byref(ar), 1000, _lib.BF16, 0, 4, None) == _lib.ERR_INVALID_ARG
+    assert lib.mlora_ar_wait(ctypes.byref(ar), None) == _lib.ERR_INVALID_ARG
+    assert lib.mlora_ar_reset(ctypes.byref(ar), None) == _lib.ERR_INVALID_ARG
+    ar.rank = 2
+    assert lib.mlora_ar_wait(ctypes.byref(ar), None) == _lib.ERR_INVALID_ARG
+
+
 @pytest.mark.parametrize("ids", [
     [0, 0, 1, 1, 1, 2],
     [0, 1, 2, 0, 2, 1, 0, 1, 2],
