@@ -32,6 +32,8 @@
  *   mlora_route_*   boolean-mask routing of ids        tlora/multi_lora_linear.py:111-116
  *                   and contiguous packing              phase3_nano_batch.py:43-71
  *   mlora_gather_rows / mlora_scatter_rows  (row permutation for any-order ids)
+ *   mlora_forward_push, mlora_ar_*  per-nano-batch SUM all-reduce of the partial
+ *                   output rows (dist.all_reduce)       phase6_two_gpu_overlap.py:247-280
  */
 #ifndef MLORA_H
 #define MLORA_H
