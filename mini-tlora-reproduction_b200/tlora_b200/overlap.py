@@ -561,7 +561,7 @@ def _ksharded(args, rank, world, dev, comm_sms):
     # the same pipeline with the Y all-reduce issued from the forward epilogue
     # over peer memory (peer.PeerAllReduce) instead of NCCL
     peer_res = None
-    if world > 1:
+    if world > 1 and getattr(args, "ksharded_comm", "both") == "both":
         try:
             layer.comm = "peer"
             layer.compute.comm_sms = 0

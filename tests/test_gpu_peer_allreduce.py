@@ -93,6 +93,17 @@ def test_push_allreduce_c3_scaled(world, impl, n_nano):
     assert orc.relative_l2(to_np(got[0][rt]), Y) <= BF16_TOL
 
 
+def test_push_allreduce_fp16():
+    """fp16 partials (the reference's GPU kernels' type): same bit-exact
+    rank-order sum."""
+    _lib.clear_device_error()
+    w = workloads.build(workloads.spec("c3", scale=0.125), device=DEV, dtype=torch.float16)
+    want, got = _emulated(w, 3, "tc", 2)
+    assert _lib.device_error() == 0
+    for y in got:
+        assert y.dtype == torch.float16 and torch.equal(y, want)
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_push_allreduce_ragged(world):
     """Partial last tile and partial last 256-column block; every row and
