@@ -476,7 +476,7 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
         jp = _job_parallel(args, rank, world, dev, metric, unit)
-        ks = _ksharded(args, rank, world, dev, comm_sms)
+        ks = _ksharded(args, rank, world, dev, comm_sms, peaks_d)
         if rank != 0:
             return None
         sp = jp["sp"]
@@ -504,7 +504,7 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
         dist.destroy_process_group()
 
 
-def _ksharded(args, rank, world, dev, comm_sms):
+def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
     """The K-sharded layer with the nano-batch all-reduce pipeline: AIMD over
     the nano-batch count, the SM reservation sweep, overlap accounting, timed
     steps and the prefetched e2e loop.  Returns the summary (rank 0)."""
@@ -572,7 +572,23 @@ def _ksharded(args, rank, world, dev, comm_sms):
             pn = min(p_sweep, key=p_sweep.get)
             p_ms = _timed_med(stepper(pn), args.steps, dev)
             err = _lib.device_error()
+            # roofline of the fused compute + collective step: the slower of the
+            # rank's FLOPs at the measured sustained GEMM peak and the bytes each
+            # GPU sends over NVLink in each direction (partials to the owners,
+            # then the owners' sums: 2 (P-1)/P M d_out 2 bytes) at the measured
+            # peer-copy bandwidth of 770 GB/s per direction
+            peak_tf = float((peaks_d or {}).get("bf16_tflops_sustained", 1370.6))
+            link_gbs = 770.0
+            nvl_bytes = 2.0 * (world - 1) / world * sp.rows * sp.d_out * 2
+            t_tc = sp.flops() / world / (peak_tf * 1e12) * 1e3
+            t_nvl = nvl_bytes / (link_gbs * 1e9) * 1e3
+            target = max(t_tc, t_nvl)
             peer_res = {"n": pn, "value": round(sp.rows / (p_ms / 1000.0), 1), "ms_per_step": round(p_ms, 4),
+                        "roofline": {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "target_ms": round(target, 4),
+                                     "tensor_ms": round(t_tc, 4), "nvlink_ms": round(t_nvl, 4),
+                                     "nvlink_bytes_per_direction": int(nvl_bytes), "frac": round(target / p_ms, 4),
+                                     "peaks": f"{peak_tf} TFLOP/s bf16 sustained (measured), {link_gbs} GB/s "
+                                              "peer copy per direction (measured on the pool)"},
                         "step_tflops": round(sp.flops() / (p_ms / 1000.0) / 1e12, 1),
                         "exposed_over_compute_ms": round(p_ms - t_compute, 4),
                         "n_sweep_ms": {str(k): round(v, 4) for k, v in p_sweep.items()},
@@ -586,7 +602,10 @@ def _ksharded(args, rank, world, dev, comm_sms):
     del w
     if rank != 0:
         return None
+    peak_tf = float((peaks_d or {}).get("bf16_tflops_sustained", 1370.6))
+    t_tc = sp.flops() / world / (peak_tf * 1e12) * 1e3
     return {"value": round(sp.rows / (ms / 1000.0), 1), "ms_per_step": round(ms, 4), "scaling": "strong",
+            "tensor_bound_ms": round(t_tc, 4), "frac_of_tensor_bound": round(t_tc / ms, 4),
             "workload": f"{sp.name} one layer, backbone K-sharded over {world} GPUs",
             "rows": sp.rows, "step_tflops": round(sp.flops() / (ms / 1000.0) / 1e12, 1),
             "overlap": {"n": best_n, "comm_sms": best_k, "nccl_channels": os.environ.get("NCCL_MAX_NCHANNELS"),
