@@ -45,7 +45,7 @@ def parse():
                         "is c3, 8192 x 8192 with 32 jobs)")
     p.add_argument("--rows-scale", type=float, default=1.0,
                    help="scale the rows of every adapter (profiling captures of a smaller case)")
-    p.add_argument("--ksharded-comm", default="nccl", choices=["both", "nccl"],
+    p.add_argument("--ksharded-comm", default="both", choices=["both", "nccl"],
                    help="N > 1: time the K-sharded pipeline with NCCL's all-reduce only, or also with the "
                         "all-reduce issued from the forward epilogue over peer memory (both)")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -12,6 +12,9 @@
 // reduce-scatter issued from the GEMM epilogue plus an owner-side gather; no
 // TMA and no multicast are involved.
 #include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -99,7 +102,9 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b, int f16) {
 // 32 (l / 4) + 8 (l % 4) .. +8 of every 256-column block, so that a warp
 // reads 512 contiguous bytes of each slot and writes 512 contiguous bytes of
 // each Y row per block.  PMAX (1, 2, 4 or 8) bounds the ranks; BU blocks are
-// loaded together so that 8 16-byte loads per lane are in flight.
+// loaded together so that 8 16-byte loads per lane are in flight (16 measured
+// no faster and cost the registers that let a finish CTA sit beside a
+// mainloop CTA).
 template <int PMAX>
 __global__ void __launch_bounds__(kArThreads) k_ar_finish(const __grid_constant__ ArFinish a) {
   constexpr int BU = PMAX >= 8 ? 1 : (PMAX >= 4 ? 2 : 4);
@@ -172,6 +177,34 @@ __global__ void k_ar_wait(const __grid_constant__ ArWait w) {
 }
 
 int lt_stride_of(int n_tiles, int world) { return (n_tiles + world - 1) / world; }
+
+// The finish and wait kernels use no shared memory, yet ask for the largest
+// shared-memory carveout: an SM is configured by the first CTA placed on it,
+// and a finish CTA that lands first on an SM with a small-carveout
+// configuration would keep the mainloop CTAs (225.5 KB each) off that SM
+// until it exits.  With the largest carveout one finish CTA fits beside a
+// mainloop CTA.  Set once per kernel and device.
+cudaError_t max_carveout_once(const void* fn) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+  if (e == cudaSuccess && done.size() < 1024) done.emplace_back(fn, dev);
+  return e;
+}
+
+template <int PMAX>
+cudaError_t launch_finish(int grid, cudaStream_t s, const ArFinish& a) {
+  cudaError_t e = max_carveout_once(reinterpret_cast<const void*>(&k_ar_finish<PMAX>));
+  if (e != cudaSuccess) return e;
+  k_ar_finish<PMAX><<<grid, kArThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
 
 // Checks shared by every entry point.
 int check_ar(const mlora_peer_ar* ar) {
@@ -249,12 +282,12 @@ extern "C" int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dt
   int grid = (warps + kArThreads / 32 - 1) / (kArThreads / 32);
   if (grid > sms) grid = sms;
   cudaStream_t s = (cudaStream_t)stream;
-  if (a.world == 1) k_ar_finish<1><<<grid, kArThreads, 0, s>>>(a);
-  else if (a.world == 2) k_ar_finish<2><<<grid, kArThreads, 0, s>>>(a);
-  else if (a.world <= 4) k_ar_finish<4><<<grid, kArThreads, 0, s>>>(a);
-  else k_ar_finish<8><<<grid, kArThreads, 0, s>>>(a);
+  MLORA_CUDA_TRY(a.world == 1   ? launch_finish<1>(grid, s, a)
+                 : a.world == 2 ? launch_finish<2>(grid, s, a)
+                 : a.world <= 4 ? launch_finish<4>(grid, s, a)
+                                : launch_finish<8>(grid, s, a));
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+  return MLORA_OK;
 }
 
 extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
@@ -264,6 +297,7 @@ extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
   w.done = ar->done[ar->rank];
   w.target = unsigned(kArGroupsPerTile) * unsigned(ar->n_tiles);
   w.timeout_ns = timeout_of(ar);
+  MLORA_CUDA_TRY(max_carveout_once(reinterpret_cast<const void*>(&k_ar_wait)));
   k_ar_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
