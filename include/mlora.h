@@ -164,9 +164,10 @@ int32_t mlora_num_tiles(int64_t rows);
  * tile (8 arrivals per 256-column block and rank).  mlora_ar_finish has the
  * owner wait (bounded) until all `world` partials of each of its tiles in a
  * range have arrived, add them in rank order in fp32, and write the rounded
- * sum into the same rows of every rank's Y, adding one per 8-row group (32 per
- * tile) to every rank's completion counter.  mlora_ar_wait waits (bounded)
- * until the completion counter of this rank reaches 32 n_tiles, i.e. until
+ * sum into the same rows of every rank's Y, adding one per work unit (8 rows
+ * by up to 2048 columns: 32 ceil(d_out / 2048) per tile) to every rank's
+ * completion counter.  mlora_ar_wait waits (bounded) until the completion
+ * counter of this rank reaches 32 ceil(d_out / 2048) n_tiles, i.e. until
  * every row of its Y holds the sum.  A wait that runs out sets bit 1 of the error word and skips the
  * tile (or returns).
  *

@@ -6,8 +6,8 @@
 // t % world) and counts it in the owner's arrival counter.  Here each owner
 // waits for the `world` partials of its tiles, adds them in rank order in
 // fp32, and writes the rounded sum into the same rows of every rank's Y with
-// plain stores through peer mappings, counting each finished 8-row group in
-// every rank's completion counter.  This is the reference's per-nano-batch SUM
+// plain stores through peer mappings, counting each finished work unit (8 rows x up to
+// 2048 columns) in every rank's completion counter.  This is the reference's per-nano-batch SUM
 // all-reduce of the output rows (phase6_two_gpu_overlap.py:247-280) as one
 // reduce-scatter issued from the GEMM epilogue plus an owner-side gather; no
 // TMA and no multicast are involved.
@@ -21,11 +21,19 @@
 namespace mlora {
 namespace {
 
-constexpr int kArThreads = 256;
+constexpr int kArColBlocks = 8;  // 256-column blocks of one finisher work unit (2048 columns)
 constexpr int kArBlock = 1 << 17;          // receive block: 256 x 256 16-bit values
 constexpr int kArSlice = 256 * 64;         // one 32-column slice of a block: 256 rows x 64 bytes
 constexpr int kArRows = 8;                          // rows of one finisher work unit (one warp)
-constexpr int kArGroupsPerTile = kTileRows / kArRows;  // units per tile
+constexpr int kArGroupsPerTile = kTileRows / kArRows;  // 8-row groups per tile
+
+// finisher CTA size: 16 warps, or 8 for up to 8 ranks (whose registers would
+// not leave room for a mainloop CTA on the same SM with 16)
+template <int PMAX>
+constexpr int ar_threads() { return PMAX >= 8 ? 256 : 512; }
+
+// work units (8-row group x 2048-column chunk) per tile
+inline int ar_units_per_tile(int n_nblk) { return kArGroupsPerTile * ((n_nblk + kArColBlocks - 1) / kArColBlocks); }
 constexpr unsigned long long kArDefaultTimeoutNs = 2000000000ull;
 
 struct ArFinish {
@@ -98,7 +106,9 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b, int f16) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// One warp per (owned tile, 8-row group); lane l covers columns
+// One warp per (owned tile, 8-row group, chunk of 8 256-column blocks), so
+// that a nano-batch of a few tiles still keeps many warps per SM busy (the
+// kernel is bound by the latency of its loads); lane l covers columns
 // 32 (l / 4) + 8 (l % 4) .. +8 of every 256-column block, so that a warp
 // reads 512 contiguous bytes of each slot and writes 512 contiguous bytes of
 // each Y row per block.  PMAX (1, 2, 4 or 8) bounds the ranks; BU blocks are
@@ -106,17 +116,22 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b, int f16) {
 // no faster and cost the registers that let a finish CTA sit beside a
 // mainloop CTA).
 template <int PMAX>
-__global__ void __launch_bounds__(kArThreads) k_ar_finish(const __grid_constant__ ArFinish a) {
+__global__ void __launch_bounds__(ar_threads<PMAX>()) k_ar_finish(const __grid_constant__ ArFinish a) {
   constexpr int BU = PMAX >= 8 ? 1 : (PMAX >= 4 ? 2 : 4);
+  constexpr int kThr = ar_threads<PMAX>();
   const int lane = threadIdx.x & 31;
-  const int gw = int((blockIdx.x * kArThreads + threadIdx.x) >> 5);
-  const int nw = int((gridDim.x * kArThreads) >> 5);
-  const int units = a.n_owned * kArGroupsPerTile;
+  const int gw = int((blockIdx.x * kThr + threadIdx.x) >> 5);
+  const int nw = int((gridDim.x * kThr) >> 5);
+  const int n_cc = (a.n_nblk + kArColBlocks - 1) / kArColBlocks;
+  const int per_tile = kArGroupsPerTile * n_cc;
+  const int units = a.n_owned * per_tile;
   const int s = lane >> 2, c = lane & 3;
   const size_t slot_stride = size_t(a.lt_stride) * size_t(a.n_nblk) * kArBlock;
   for (int u = gw; u < units; u += nw) {
-    const int tile = a.t_first + (u / kArGroupsPerTile) * a.world;
-    const int rg = u % kArGroupsPerTile;
+    const int tile = a.t_first + (u / per_tile) * a.world;
+    const int rg = (u % per_tile) / n_cc;
+    const int b_lo = (u % n_cc) * kArColBlocks;
+    const int b_hi = min(b_lo + kArColBlocks, a.n_nblk);
     const int lt = tile / a.world;
     if (lt >= a.lt_stride) {  // cannot happen for a range inside the layout
       if (lane == 0) atomicOr(&g_err_word, kErrBounds);
@@ -132,12 +147,12 @@ __global__ void __launch_bounds__(kArThreads) k_ar_finish(const __grid_constant_
       const int r = rg * kArRows + j;
       const int64_t row = int64_t(tile) * kTileRows + r;
       if (row >= a.M) break;
-      for (int b0 = 0; b0 < a.n_nblk; b0 += BU) {
+      for (int b0 = b_lo; b0 < b_hi; b0 += BU) {
         uint4 v[BU][PMAX];
 #pragma unroll
         for (int q = 0; q < BU; ++q) {
           const int col = (b0 + q) * 256 + s * 32 + c * 8;
-          if (b0 + q < a.n_nblk && col < a.d_out) {  // d_out % 8 == 0: an 8-column chunk is whole or absent
+          if (b0 + q < b_hi && col < a.d_out) {  // d_out % 8 == 0: an 8-column chunk is whole or absent
             const uint8_t* src = base + size_t(b0 + q) * kArBlock + r * 64;
 #pragma unroll
             for (int p = 0; p < PMAX; ++p)
@@ -147,7 +162,7 @@ __global__ void __launch_bounds__(kArThreads) k_ar_finish(const __grid_constant_
 #pragma unroll
         for (int q = 0; q < BU; ++q) {
           const int col = (b0 + q) * 256 + s * 32 + c * 8;
-          if (b0 + q >= a.n_nblk || col >= a.d_out) continue;
+          if (b0 + q >= b_hi || col >= a.d_out) continue;
           float acc[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -202,7 +217,7 @@ template <int PMAX>
 cudaError_t launch_finish(int grid, cudaStream_t s, const ArFinish& a) {
   cudaError_t e = max_carveout_once(reinterpret_cast<const void*>(&k_ar_finish<PMAX>));
   if (e != cudaSuccess) return e;
-  k_ar_finish<PMAX><<<grid, kArThreads, 0, s>>>(a);
+  k_ar_finish<PMAX><<<grid, ar_threads<PMAX>(), 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -278,8 +293,9 @@ extern "C" int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dt
   int dev = 0, sms = 0;
   MLORA_CUDA_TRY(cudaGetDevice(&dev));
   MLORA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int warps = a.n_owned * kArGroupsPerTile;
-  int grid = (warps + kArThreads / 32 - 1) / (kArThreads / 32);
+  const int warps = a.n_owned * ar_units_per_tile(a.n_nblk);
+  const int per_cta = (a.world <= 4 ? ar_threads<4>() : ar_threads<8>()) / 32;
+  int grid = (warps + per_cta - 1) / per_cta;
   if (grid > sms) grid = sms;
   cudaStream_t s = (cudaStream_t)stream;
   MLORA_CUDA_TRY(a.world == 1   ? launch_finish<1>(grid, s, a)
@@ -295,7 +311,7 @@ extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
   if (st != MLORA_OK) return st;
   ArWait w;
   w.done = ar->done[ar->rank];
-  w.target = unsigned(kArGroupsPerTile) * unsigned(ar->n_tiles);
+  w.target = unsigned(ar_units_per_tile((ar->d_out + 255) / 256)) * unsigned(ar->n_tiles);
   w.timeout_ns = timeout_of(ar);
   MLORA_CUDA_TRY(max_carveout_once(reinterpret_cast<const void*>(&k_ar_wait)));
   k_ar_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);
