@@ -6,9 +6,10 @@ stream, beside the next nano-batch's mainloops.  Every finish starts after
 all the pushes it waits for, so no kernel waits on a kernel running beside it.
 
 Prints one JSON line: per nano-batch count N, the device milliseconds of the
-pushes alone, of pushes + finishes in sequence, and of pushes + finishes
-overlapped; and of one finish of all tiles alone.  The emulated GPU does the
-work of every rank, so the times are ``world`` times a rank's share.
+plain mainloops (writing a local Y, no all-reduce), of the pushes alone, of
+pushes + finishes in sequence, and of pushes + finishes overlapped; and of one
+finish of all tiles alone.  The emulated GPU does the work of every rank, so
+the times are ``world`` times a rank's share.
 
     python -m tlora_b200.peer_bench --workload c3 --world 2 --rows-scale 1.0
 """
@@ -48,7 +49,15 @@ def main():
     main_s = torch.cuda.current_stream()
     side = torch.cuda.Stream()
 
+    ys = [torch.empty(rows, d_out, dtype=w.x.dtype, device=dev) for _ in range(world)]
+
     def run(n, mode):
+        if mode == "main_only":
+            for t0, t1 in split_ranges(n_tiles, n):
+                for r, (L, c) in enumerate(zip(layers, ctxs)):
+                    c["fw"].y = ys[r]
+                    L.compute.main(c, t0, t1, expand=r == 0, add_bias=r == 0)
+            return
         for a in ars:
             a.reset(main_s)
         for t0, t1 in split_ranges(n_tiles, n):
@@ -89,7 +98,7 @@ def main():
     out = {"workload": f"{w.spec.name} rows={rows} d_out={d_out}, {world} ranks emulated on one GPU", "ms": {}}
     for n in (int(v) for v in args.nano.split(",")):
         out["ms"][str(n)] = {m: round(timed(lambda: run(n, m), args.iters), 4)
-                             for m in ("push_only", "serial", "overlap")}
+                             for m in ("main_only", "push_only", "serial", "overlap")}
 
     # one finish of all tiles by every rank, its pushes complete
     run(1, "push_only")
