@@ -226,12 +226,9 @@ class ShardedLayer:
 
     def peer_buffers(self, rows: int, dtype, device) -> "peer.PeerAllReduce":
         """This rank's peer all-reduce buffers for ``rows`` rows (collective
-        on first use or when the row count changes)."""
-        if self._ar is None or self._ar.rows != rows:
-            if self._ar is not None:
-                torch.cuda.synchronize(device)
-                dist.barrier(group=self.group)  # no rank still writes into the old buffers
-                self._ar.close()
+        on first use or when the row count or dtype changes)."""
+        if self._ar is None or self._ar.rows != rows or self._ar.dtype != dtype:
+            self.close()  # no rank still uses the old buffers; every rank unmaps before any frees
             d_out = self.B_pack.shape[0]
             self._ar = peer.PeerAllReduce.over_group(rows, d_out, dtype, device, self.group)
             self._one = torch.zeros(1, dtype=torch.float32, device=device)
