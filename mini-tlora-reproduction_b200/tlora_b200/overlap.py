@@ -168,6 +168,9 @@ class ShardedLayer:
         self.comm = comm
         self._ar = None
         self._last_done = None
+        # set to a list to record a timeline of the next steps: (phase, CUDA
+        # event on the stream that runs it); read with timeline_ms()
+        self.timeline = None
         self.bwd_group = bwd_group if bwd_group is not None else group
         A_pack, B_pack, table = model.packed()
         d_in = model.base.in_features
@@ -180,6 +183,21 @@ class ShardedLayer:
         self.table = table
         self.scaling = np.array([float(a.scaling) for a in model.adapters.values()], dtype=np.float32)
         self.compute = compute or NativeCompute(getattr(model, "impl", "auto"))
+
+    def _mark(self, name: str, stream=None) -> None:
+        if self.timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            self.timeline.append((name, ev))
+
+    def timeline_ms(self) -> dict:
+        """Milliseconds from the first recorded phase to the end of each
+        recorded phase (waits for the device)."""
+        if not self.timeline:
+            return {}
+        torch.cuda.synchronize()
+        t0 = self.timeline[0][1]
+        return {name: round(t0.elapsed_time(ev), 4) for name, ev in self.timeline}
 
     def shard_input(self, x: torch.Tensor) -> torch.Tensor:
         return x[:, self.k0:self.k1].contiguous()
@@ -200,9 +218,11 @@ class ShardedLayer:
         if comm and pipelined and self.comm == "peer" and self.world > 1:
             return self._forward_peer(x_p, plan, n_nano)
         c = self.compute
+        self._mark("start")
         ctx = c.begin(self, x_p, plan)
         with _Range("mlora.shrink"):
             c.shrink(ctx)
+        self._mark("shrink")
         hz = None
         if comm and ctx["z"] is not None:
             hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
@@ -215,6 +235,7 @@ class ShardedLayer:
         for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
             with _Range(f"mlora.nano{i}"):
                 c.main(ctx, t0, t1, expand=owner, add_bias=owner)
+                self._mark(f"main{i}")
                 if not comm:
                     continue
                 seg = ctx["y"][t0 * TILE_ROWS:min(t1 * TILE_ROWS, rows)]
@@ -249,13 +270,16 @@ class ShardedLayer:
         cur = torch.cuda.current_stream(dev)
         if self._last_done is not None:
             cur.wait_event(self._last_done)  # this rank's previous call is finished with the buffers
+        self._mark("start")
         ar.reset(cur)
         # every rank's counters are zero before any rank pushes (and every
         # rank's previous call has finished with the buffers)
         dist.all_reduce(self._one, op=dist.ReduceOp.SUM, group=self.group)
+        self._mark("barrier")
         ctx = c.begin(self, x_p, plan, y=ar.y)
         with _Range("mlora.shrink"):
             c.shrink(ctx)
+        self._mark("shrink")
         hz = None
         if ctx["z"] is not None:
             hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
@@ -267,11 +291,14 @@ class ShardedLayer:
         for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
             with _Range(f"mlora.nano{i}"):
                 c.push(ctx, ar, t0, t1, expand=owner, add_bias=owner)
+                self._mark(f"push{i}", cur)
                 ev = torch.cuda.Event()
                 ev.record(cur)
                 side.wait_event(ev)
                 ar.finish(t0, t1, side)
+                self._mark(f"finish{i}", side)
         ar.wait(side)
+        self._mark("ar_wait", side)
         done = torch.cuda.Event()
         done.record(side)
         self._last_done = done
@@ -300,13 +327,17 @@ class ShardedLayer:
         b = c.bwd_begin(ctx, self, x_p, dy, overlapped)
         t0, t1 = _share(b["n_tiles"], self.rank, self.world)
         c.bwd_dz(b, t0, t1)
+        self._mark("bwd_dz")
         if b["dz"] is not None and self.world > 1:
             dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.bwd_group)
+            self._mark("bwd_dz_allreduce")
         c.bwd_dx_da(b)
+        self._mark("bwd_dx_da")
         b0, b1 = _share(b["n_db"], self.rank, self.world)
         c.bwd_db(b, b0, b1)
         if self.world > 1:
             dist.all_reduce(b["dB"], op=dist.ReduceOp.SUM, group=self.bwd_group)
+        self._mark("bwd_db")
         return b["dx"], b["dA"], b["dB"]
 
     def step(self, x_p, plan, dy, n_nano: int, lr: float, pipelined: bool = True, comm: bool = True):
@@ -322,8 +353,10 @@ class ShardedLayer:
             dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works))
         with _Range("mlora.sgd"):
             self.compute.sgd(self, plan, dA_p, dB, lr)
+        self._mark("sgd")
         for w in works:
             w.wait()
+        self._mark("end")
         return y, dx_p
 
 
@@ -501,6 +534,18 @@ def bench_multi(args, peaks_d, peaks_kind, metric, unit):
         dist.destroy_process_group()
 
 
+def _one_timeline(layer: ShardedLayer, step, device) -> dict:
+    """One step with the layer's phase timeline on: milliseconds from the
+    step's start to the end of each phase on this rank."""
+    torch.cuda.synchronize(device)
+    layer.timeline = []
+    try:
+        step()
+        return layer.timeline_ms()
+    finally:
+        layer.timeline = None
+
+
 def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
     """The K-sharded layer with the nano-batch all-reduce pipeline: AIMD over
     the nano-batch count, the SM reservation sweep, overlap accounting, timed
@@ -554,6 +599,7 @@ def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
     t_comm = _timed_med(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev)
     hidden = 1.0 - max(0.0, t_pipe - t_compute) / t_comm if t_comm > 0 else 0.0
     ms = _timed_med(stepper(best_n), args.steps, dev)
+    timeline = _one_timeline(layer, stepper(best_n), dev)
 
     # the same pipeline with the Y all-reduce issued from the forward epilogue
     # over peer memory (peer.PeerAllReduce) instead of NCCL
@@ -568,6 +614,7 @@ def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
             p_sweep = {n: _timed_med(stepper(n), 3, dev) for n in (1, 2, 4, 8, 16) if n <= n_tiles}
             pn = min(p_sweep, key=p_sweep.get)
             p_ms = _timed_med(stepper(pn), args.steps, dev)
+            p_timeline = _one_timeline(layer, stepper(pn), dev)
             err = _lib.device_error()
             # roofline of the fused compute + collective step: the slower of the
             # rank's FLOPs at the measured sustained GEMM peak and the bytes each
@@ -589,6 +636,7 @@ def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
                         "step_tflops": round(sp.flops() / (p_ms / 1000.0) / 1e12, 1),
                         "exposed_over_compute_ms": round(p_ms - t_compute, 4),
                         "n_sweep_ms": {str(k): round(v, 4) for k, v in p_sweep.items()},
+                        "timeline_ms": p_timeline,
                         "device_error": int(err)}
         except Exception as e:  # reported beside the NCCL numbers, which stand
             peer_res = {"error": f"{type(e).__name__}: {e}"[:300]}
@@ -612,4 +660,5 @@ def _ksharded(args, rank, world, dev, comm_sms, peaks_d=None):
                         "comm_hidden_frac": round(hidden, 4)},
             "n_sweep_ms": {str(k): round(v, 4) for k, v in n_sweep.items()},
             "aimd": horizons,
+            "timeline_ms": timeline,
             "peer_allreduce": peer_res}
