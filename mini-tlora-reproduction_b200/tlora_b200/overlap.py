@@ -541,7 +541,10 @@ def _one_timeline(layer: ShardedLayer, step, device) -> dict:
     layer.timeline = []
     try:
         step()
-        return layer.timeline_ms()
+        try:
+            return layer.timeline_ms()
+        except Exception as e:  # a timing record only: never fail the bench over it
+            return {"error": f"{type(e).__name__}: {e}"[:200]}
     finally:
         layer.timeline = None
 
