@@ -1,7 +1,7 @@
 """GPU parity: the native kernels against the numpy oracle (and, for the
 reference's own test cases, against the reference's golden outputs).
 
-Tolerances (north star): relative L2 <= 1e-5 in fp32 mode, <= 2e-2 in bf16
+Tolerances: relative L2 <= 1e-5 in fp32 mode, <= 2e-2 in bf16
 mode (fp32 accumulation), for Y, dX, dA, dB and the one-step SGD update.
 """
 

@@ -48,7 +48,7 @@ def test_backward_and_sgd_match_reference(golden_dir, name):
     for a in ads:
         if f"dA_{a}" in z:
             # the reference accumulates in fp32, the oracle in fp64: pin by
-            # relative L2 (north-star fp32 bound 1e-5) plus an absolute 2e-5,
+            # relative L2 (the fp32 bound 1e-5) plus an absolute 2e-5,
             # the gradient tolerance of phase4_aimd.py:143-147
             for got, key in ((dA[a], f"dA_{a}"), (dB[a], f"dB_{a}")):
                 assert orc.relative_l2(got, z[key]) <= 1e-5
