@@ -168,6 +168,7 @@ class ShardedLayer:
         self.comm = comm
         self._ar = None
         self._last_done = None
+        self._pending = None  # the peer all-reduce's last finish, until launched
         # set to a list to record a timeline of the next steps: (phase, CUDA
         # event on the stream that runs it); read with timeline_ms()
         self.timeline = None
@@ -212,11 +213,15 @@ class ShardedLayer:
             hz.wait()
         return y, ctx
 
-    def forward_async(self, x_p, plan, n_nano: int, pipelined: bool = True, comm: bool = True):
+    def forward_async(self, x_p, plan, n_nano: int, pipelined: bool = True, comm: bool = True,
+                      defer_finish: bool = False):
         """Pipelined forward that returns with the nano-batch all-reduces still
-        in flight: (Y, ctx, Y work handles, Z work handle or None)."""
+        in flight: (Y, ctx, Y work handles, Z work handle or None).  With the
+        peer all-reduce and ``defer_finish``, the last nano-batch's finish is
+        launched by the returned handle's ``launch()`` (or its ``wait()``), so
+        that the caller can queue it beside work of its choice."""
         if comm and pipelined and self.comm == "peer" and self.world > 1:
-            return self._forward_peer(x_p, plan, n_nano)
+            return self._forward_peer(x_p, plan, n_nano, defer_finish)
         c = self.compute
         self._mark("start")
         ctx = c.begin(self, x_p, plan)
@@ -256,7 +261,7 @@ class ShardedLayer:
             self._side = torch.cuda.Stream(device)
         return self._ar
 
-    def _forward_peer(self, x_p, plan, n_nano: int):
+    def _forward_peer(self, x_p, plan, n_nano: int, defer_finish: bool = False):
         """forward_async with the Y all-reduce issued from the forward epilogue
         (peer.PeerAllReduce); the returned work handle makes the caller's
         stream wait until every row of Y holds the sum.  Y is the peer buffer
@@ -267,6 +272,8 @@ class ShardedLayer:
         dev = x_p.device
         rows = x_p.shape[0]
         ar = self.peer_buffers(rows, x_p.dtype, dev)
+        if self._pending is not None:
+            self._pending.launch()  # a previous call's deferred finish that nobody launched
         cur = torch.cuda.current_stream(dev)
         if self._last_done is not None:
             cur.wait_event(self._last_done)  # this rank's previous call is finished with the buffers
@@ -288,21 +295,22 @@ class ShardedLayer:
             hz.wait()
             hz = None
         side = self._side
-        for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
+        ranges = split_ranges(ctx["n_tiles"], n_nano)
+        for i, (t0, t1) in enumerate(ranges):
             with _Range(f"mlora.nano{i}"):
                 c.push(ctx, ar, t0, t1, expand=owner, add_bias=owner)
                 self._mark(f"push{i}", cur)
-                ev = torch.cuda.Event()
-                ev.record(cur)
-                side.wait_event(ev)
-                ar.finish(t0, t1, side)
-                self._mark(f"finish{i}", side)
-        ar.wait(side)
-        self._mark("ar_wait", side)
-        done = torch.cuda.Event()
-        done.record(side)
-        self._last_done = done
-        return ar.y, ctx, [_EventWork(done, dev)], hz
+                if i + 1 < len(ranges):
+                    ev = torch.cuda.Event()
+                    ev.record(cur)
+                    side.wait_event(ev)
+                    ar.finish(t0, t1, side)
+                    self._mark(f"finish{i}", side)
+        last = _PeerFinish(self, ar, ranges[-1], len(ranges) - 1, dev)
+        self._pending = last
+        if not defer_finish:
+            last.launch()
+        return ar.y, ctx, [last], hz
 
     def close(self) -> None:
         """Release the peer buffers (collective: every rank calls it after its
@@ -317,8 +325,9 @@ class ShardedLayer:
         self._ar.close()
         self._ar = None
         self._last_done = None
+        self._pending = None
 
-    def backward(self, ctx, x_p, dy, overlapped=False):
+    def backward(self, ctx, x_p, dy, overlapped=False, after_dz=None):
         """Backward on this rank's shard.  dZ (needs all of dY and B) and dB
         (needs all of dY and Z) are split across ranks — dZ by tiles, dB by
         128-row blocks of d_out — and summed with two small all-reduces;
@@ -331,6 +340,8 @@ class ShardedLayer:
         if b["dz"] is not None and self.world > 1:
             dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.bwd_group)
             self._mark("bwd_dz_allreduce")
+        if after_dz is not None:
+            after_dz()
         c.bwd_dx_da(b)
         self._mark("bwd_dx_da")
         b0, b1 = _share(b["n_db"], self.rank, self.world)
@@ -346,11 +357,19 @@ class ShardedLayer:
         the following nano-batches AND the backward: dY is the upstream
         gradient, so the backward needs only the (small) all-reduced Z; the
         Y all-reduces are waited for at the end of the step."""
-        y, ctx, works, hz = self.forward_async(x_p, plan, n_nano, pipelined, comm)
+        y, ctx, works, hz = self.forward_async(x_p, plan, n_nano, pipelined, comm, defer_finish=True)
         if hz is not None:
             hz.wait()  # dB = dY^T Z needs the summed Z
+
+        def after_dz():
+            # the peer all-reduce's last finish (HBM-bound) runs beside the
+            # tensor-bound dX mainloop rather than beside the HBM-bound dZ pass
+            for w in works:
+                if isinstance(w, _PeerFinish):
+                    w.launch()
+
         with _Range("mlora.backward"):
-            dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works))
+            dx_p, dA_p, dB = self.backward(ctx, x_p, dy, overlapped=bool(works), after_dz=after_dz)
         with _Range("mlora.sgd"):
             self.compute.sgd(self, plan, dA_p, dB, lr)
         self._mark("sgd")
@@ -360,16 +379,37 @@ class ShardedLayer:
         return y, dx_p
 
 
-class _EventWork:
-    """Work handle of the peer all-reduce: wait() makes the current stream
-    wait for the side stream's completion event (as an NCCL work handle's
-    wait() does for its collective)."""
+class _PeerFinish:
+    """Work handle of the peer all-reduce: the last nano-batch's finish and
+    the completion wait, queued on the layer's side stream by ``launch()``
+    (after the work queued so far on the current stream), and ``wait()``,
+    which launches them if that has not happened and makes the current stream
+    wait for them (as an NCCL work handle's wait() does for its collective)."""
 
-    def __init__(self, ev: torch.cuda.Event, device):
-        self.ev, self.device = ev, device
+    def __init__(self, layer: "ShardedLayer", ar, rng, index: int, device):
+        self.layer, self.ar, self.rng, self.index, self.device = layer, ar, rng, index, device
+        self.done = None
+
+    def launch(self):
+        if self.done is not None:
+            return
+        L, side = self.layer, self.layer._side
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        side.wait_event(ev)
+        self.ar.finish(self.rng[0], self.rng[1], side)
+        L._mark(f"finish{self.index}", side)
+        self.ar.wait(side)
+        L._mark("ar_wait", side)
+        self.done = torch.cuda.Event()
+        self.done.record(side)
+        L._last_done = self.done
+        if L._pending is self:
+            L._pending = None
 
     def wait(self):
-        torch.cuda.current_stream(self.device).wait_event(self.ev)
+        self.launch()
+        torch.cuda.current_stream(self.device).wait_event(self.done)
 
 
 def comm_only(layer: ShardedLayer, y: torch.Tensor, z: Optional[torch.Tensor], n_tiles: int, n_nano: int):
