@@ -21,6 +21,14 @@
  * entry point takes an explicit stream and allocates nothing on the hot path.
  * Routing arrays (mlora_routing) are HOST arrays.
  *
+ * Alignment: the tensor-core kernels read and write every tensor (X, W, bias,
+ * A_pack, B_pack, Y, the save buffers, dY, dX, dA_pack, dB_pack) with TMA or
+ * 16-byte vector accesses, so their base addresses must be 16-byte aligned.
+ * With MLORA_IMPL_AUTO a call whose pointers are not runs on the CUDA-core
+ * kernels (element-aligned accesses); with MLORA_IMPL_TC* it returns
+ * MLORA_ERR_UNSUPPORTED before launching anything.  Every pointer must be
+ * aligned to its element size.
+ *
  * Reference interfaces replaced (GOPIKA-SUSHAMA/mini-tlora-reproduction):
  *   mlora_forward   MultiLoRALinear.forward          tlora/multi_lora_linear.py:92-118
  *                   fused_full_forward (cuBLAS base + fused_lora_residual_kernel,
@@ -83,6 +91,13 @@ typedef struct mlora_problem {
                        communication kernels running at the same time (the
                        nano-batch all-reduce overlap). */
   int32_t flags;    /* MLORA_PLAN_* below; 0 by default */
+  int32_t* err_word; /* optional DEVICE int32 owned by the caller: the device-side checks of this
+                        call's kernels (bit 0 = a bounds check fired, bit 1 = a bounded wait timed
+                        out) are OR-ed into it, so that calls running at the same time on several
+                        streams or threads each see only their own flags.  The library never clears
+                        it.  NULL = the library-wide word of mlora_get_error.  Replaces the
+                        exception a failing kernel raises through torch in the reference
+                        (phase5c_fused_triton.py:524-540); no counterpart otherwise. */
 } mlora_problem;
 /* flags: the workspace already holds this problem's routing plan, written by
  * mlora_plan_upload with the same problem and routing; the call then issues
@@ -188,7 +203,10 @@ typedef struct mlora_peer_ar {
   uint32_t* arrive[MLORA_AR_MAX_RANKS];  /* rank r's arrival counters (mlora_ar_layout) */
   void* y[MLORA_AR_MAX_RANKS];           /* rank r's Y [rows, d_out] */
   uint32_t* done[MLORA_AR_MAX_RANKS];    /* rank r's completion counter */
-  int64_t timeout_ns;                    /* bound of each device-side wait; 0 = 2 s */
+  int64_t timeout_ns;                    /* bound of all device-side waits of one launch together
+                                            (one deadline per launch); 0 = 2 s */
+  int32_t* err_word;                     /* optional DEVICE int32 for this rank's flags (as
+                                            mlora_problem.err_word); NULL = the library-wide word */
 } mlora_peer_ar;
 
 /* Bytes of one rank's receive buffer and of its counters (arrival counters
@@ -230,7 +248,9 @@ int mlora_ipc_close(void* ptr);
  *    MLORA_ERR_WORKSPACE and launches nothing.
  *  - The first call on each device looks the array's address up
  *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture on the device.
+ *    before any stream capture on the device.  The address is kept for the
+ *    process; after a cudaDeviceReset of that device it is stale, so do not
+ *    call this entry point on a device after resetting it.
  *  - All calls on a device share the array and it keeps the last call's
  *    contents; each call writes all the scratch it reads, but calls that
  *    overlap on the GPU (several streams or host threads at once) race and
@@ -315,8 +335,9 @@ int mlora_gather_rows(const void* src, const int32_t* perm, int64_t rows, int32_
 int mlora_scatter_rows(const void* src, const int32_t* perm, int64_t rows, int32_t cols,
                        int32_t dtype, void* dst, void* stream);
 
-/* Device error word of this library on the current device: bit 0 = a bounds
- * check fired, bit 1 = a bounded wait timed out.  mlora_clear_error resets it. */
+/* Library-wide device error word on the current device: bit 0 = a bounds
+ * check fired, bit 1 = a bounded wait timed out.  Only calls made with a NULL
+ * err_word report into it.  mlora_clear_error resets it. */
 int mlora_get_error(int32_t* flags);
 int mlora_clear_error(void);
 

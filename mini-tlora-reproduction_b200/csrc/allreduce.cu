@@ -42,7 +42,8 @@ struct ArFinish {
   int f16;
   int64_t M;
   unsigned arrive_target;  // world * 8 * n_nblk
-  unsigned long long timeout_ns;
+  unsigned long long timeout_ns;  // bound of all the launch's waits together
+  int* err;                       // this rank's status word, or nullptr for the library-wide word
   const uint8_t* recv;
   const unsigned* arrive;
   uint8_t* y[MLORA_AR_MAX_RANKS];
@@ -53,6 +54,7 @@ struct ArWait {
   const unsigned* done;
   unsigned target;
   unsigned long long timeout_ns;
+  int* err;
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -68,14 +70,16 @@ __device__ __forceinline__ unsigned long long ar_now() {
 }
 
 // Whole warp: wait until *c >= target (every lane reads the counter with
-// acquire semantics), at most timeout_ns.  Returns false on timeout.
-__device__ bool ar_wait_count(const unsigned* c, unsigned target, unsigned long long timeout_ns) {
-  const unsigned long long t0 = ar_now();
+// acquire semantics), at most until the global timer passes `deadline`.
+// Returns false on timeout.  One deadline serves all the waits of a warp, so
+// a launch whose partials never arrive returns after one timeout, however
+// many work units each warp holds.
+__device__ bool ar_wait_count(const unsigned* c, unsigned target, unsigned long long deadline) {
   unsigned nap = 64;
   for (;;) {
     const bool ready = ld_acquire_sys(c) >= target;
     if (__all_sync(0xffffffffu, ready)) return true;
-    const bool late = __shfl_sync(0xffffffffu, ar_now() - t0 > timeout_ns ? 1 : 0, 0) != 0;
+    const bool late = __shfl_sync(0xffffffffu, ar_now() > deadline ? 1 : 0, 0) != 0;
     if (late) return false;
     __nanosleep(nap);
     if (nap < 2048) nap *= 2;
@@ -127,6 +131,8 @@ __global__ void __launch_bounds__(ar_threads<PMAX>()) k_ar_finish(const __grid_c
   const int units = a.n_owned * per_tile;
   const int s = lane >> 2, c = lane & 3;
   const size_t slot_stride = size_t(a.lt_stride) * size_t(a.n_nblk) * kArBlock;
+  // lane 0's clock, shared by the warp: every wait of this warp ends by then
+  const unsigned long long deadline = __shfl_sync(0xffffffffu, ar_now(), 0) + a.timeout_ns;
   for (int u = gw; u < units; u += nw) {
     const int tile = a.t_first + (u / per_tile) * a.world;
     const int rg = (u % per_tile) / n_cc;
@@ -134,12 +140,12 @@ __global__ void __launch_bounds__(ar_threads<PMAX>()) k_ar_finish(const __grid_c
     const int b_hi = min(b_lo + kArColBlocks, a.n_nblk);
     const int lt = tile / a.world;
     if (lt >= a.lt_stride) {  // cannot happen for a range inside the layout
-      if (lane == 0) atomicOr(&g_err_word, kErrBounds);
+      if (lane == 0) flag_error(a.err, kErrBounds);
       continue;
     }
-    if (!ar_wait_count(a.arrive + lt, a.arrive_target, a.timeout_ns)) {
+    if (!ar_wait_count(a.arrive + lt, a.arrive_target, deadline)) {
       // no completion count for this group: every rank waiting for it times out too
-      if (lane == 0) atomicOr(&g_err_word, kErrTimeout);
+      if (lane == 0) flag_error(a.err, kErrTimeout);
       continue;
     }
     const uint8_t* base = a.recv + size_t(lt) * size_t(a.n_nblk) * kArBlock + s * kArSlice + c * 16;
@@ -188,7 +194,8 @@ __global__ void __launch_bounds__(ar_threads<PMAX>()) k_ar_finish(const __grid_c
 }
 
 __global__ void k_ar_wait(const __grid_constant__ ArWait w) {
-  if (!ar_wait_count(w.done, w.target, w.timeout_ns) && threadIdx.x == 0) atomicOr(&g_err_word, kErrTimeout);
+  const unsigned long long deadline = __shfl_sync(0xffffffffu, ar_now(), 0) + w.timeout_ns;
+  if (!ar_wait_count(w.done, w.target, deadline) && threadIdx.x == 0) flag_error(w.err, kErrTimeout);
 }
 
 int lt_stride_of(int n_tiles, int world) { return (n_tiles + world - 1) / world; }
@@ -284,6 +291,7 @@ extern "C" int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dt
   if (a.n_owned == 0) return MLORA_OK;
   a.arrive_target = unsigned(ar->world) * 8u * unsigned(a.n_nblk);
   a.timeout_ns = timeout_of(ar);
+  a.err = ar->err_word;
   a.recv = static_cast<const uint8_t*>(ar->recv[ar->rank]);
   a.arrive = ar->arrive[ar->rank];
   for (int r = 0; r < ar->world; ++r) {
@@ -313,6 +321,7 @@ extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
   w.done = ar->done[ar->rank];
   w.target = unsigned(ar_units_per_tile((ar->d_out + 255) / 256)) * unsigned(ar->n_tiles);
   w.timeout_ns = timeout_of(ar);
+  w.err = ar->err_word;
   MLORA_CUDA_TRY(max_carveout_once(reinterpret_cast<const void*>(&k_ar_wait)));
   k_ar_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);
   count_launch();

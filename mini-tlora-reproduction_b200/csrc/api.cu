@@ -1,6 +1,7 @@
 // C-ABI entry points (include/mlora.h): argument checks, plan upload and
 // dispatch between the tcgen05 tensor-core family and the SIMT family.
 #include <cstring>
+#include <initializer_list>
 
 #include "common.cuh"
 #include "simt.cuh"
@@ -70,9 +71,22 @@ int view_plan(const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
   return MLORA_OK;
 }
 
-// Plan of a call: uploaded now, or already resident in the workspace.
+// Plan of a call: uploaded now, or already resident in the workspace; the
+// kernels report their device-side checks into the call's status word.
 int stage_plan(const mlora_problem* prob, const Plan& p, void* ws, cudaStream_t st, PlanDev* dev) {
-  return (prob->flags & MLORA_PLAN_RESIDENT) ? view_plan(p, ws, st, dev) : upload_plan(p, ws, st, dev);
+  const int s = (prob->flags & MLORA_PLAN_RESIDENT) ? view_plan(p, ws, st, dev) : upload_plan(p, ws, st, dev);
+  dev->err = prob->err_word;
+  return s;
+}
+
+// Every tensor pointer of a call meets the alignment of the kernel family:
+// 16 bytes for the tensor-core kernels (TMA boxes, 16-byte vector loads of
+// the bias and stores of dB / the intermediates), the element size for the
+// CUDA-core kernels.
+bool pointers_aligned(std::initializer_list<const void*> ptrs, size_t a) {
+  for (const void* q : ptrs)
+    if (!aligned(q, a)) return false;
+  return true;
 }
 
 bool tc_shape_ok(const mlora_problem* prob) {
@@ -80,12 +94,17 @@ bool tc_shape_ok(const mlora_problem* prob) {
   return (prob->dtype == MLORA_BF16 || prob->dtype == MLORA_F16) && prob->d_in % 8 == 0 && prob->d_out % 8 == 0;
 }
 
-int choose_impl(const mlora_problem* prob) {
+// Kernel family of a call whose tensor pointers are `ptrs`; -1 = unsupported
+// (an explicit tensor-core request with a shape or pointer the tensor-core
+// kernels cannot take, or pointers not aligned to their element size).
+int choose_impl(const mlora_problem* prob, std::initializer_list<const void*> ptrs) {
+  if (!pointers_aligned(ptrs, size_t(elem_bytes(prob->dtype)))) return -1;
+  const bool tc_ok = tc_shape_ok(prob) && pointers_aligned(ptrs, 16);
   if (prob->impl == MLORA_IMPL_SIMT) return MLORA_IMPL_SIMT;
   if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM || prob->impl == MLORA_IMPL_TC_2SM)
-    return tc_shape_ok(prob) ? MLORA_IMPL_TC : -1;
+    return tc_ok ? MLORA_IMPL_TC : -1;
   if (prob->impl != MLORA_IMPL_AUTO) return -1;
-  return (tc_shape_ok(prob) && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
+  return (tc_ok && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
 }
 
 }  // namespace
@@ -117,6 +136,7 @@ extern "C" int mlora_plan_upload(const mlora_problem* prob, const mlora_routing*
   int st = build_plan(prob, route, &p);
   if (st != MLORA_OK) return st;
   if (!workspace) return MLORA_ERR_INVALID_ARG;
+  if (!aligned(workspace, 16)) return MLORA_ERR_UNSUPPORTED;
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
   PlanDev dev;
   return upload_plan(p, workspace, (cudaStream_t)stream, &dev);
@@ -149,7 +169,8 @@ int forward_staged(const mlora_problem* prob, const mlora_routing* route, const 
   if (need_z && (stages & MLORA_STAGE_MAIN) && !(stages & MLORA_STAGE_NO_EXPAND) && !B_pack)
     return MLORA_ERR_INVALID_ARG;
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
-  const int impl = choose_impl(prob);
+  if (!aligned(workspace, 16)) return MLORA_ERR_UNSUPPORTED;  // plan tables hold 16-byte entries
+  const int impl = choose_impl(prob, {X, W, bias, A_pack, B_pack, Y, zsave});
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
   if (ar && (impl != MLORA_IMPL_TC || route->out_rows)) return MLORA_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
@@ -246,7 +267,8 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
   if (((dA_pack && (stages & MLORA_BWD_DA)) || (dB_pack && (stages & MLORA_BWD_DB))) && !X)
     return MLORA_ERR_INVALID_ARG;
   if (workspace_bytes < ws_bytes(p, prob->dtype)) return MLORA_ERR_WORKSPACE;
-  const int impl = choose_impl(prob);
+  if (!aligned(workspace, 16)) return MLORA_ERR_UNSUPPORTED;  // plan tables hold 16-byte entries
+  const int impl = choose_impl(prob, {dY, X, W, A_pack, B_pack, zsave, dzsave, dX, dA_pack, dB_pack});
   if (impl < 0) return MLORA_ERR_UNSUPPORTED;
   cudaStream_t s = (cudaStream_t)stream;
   PlanDev dev;

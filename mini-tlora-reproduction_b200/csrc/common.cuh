@@ -61,6 +61,8 @@ struct PlanDev {
   const int4* list_desc;            // [n_list] {base chunk, tile, first 64-row slice, one past the last}
   int32_t* counters;                // [16] work counters of the persistent kernels, one per role;
                                     // zeroed by every plan upload (one per API call)
+  int* err;                         // status word of this call (mlora_problem.err_word), or nullptr
+                                    // for the library-wide word g_err_word
 };
 
 // Host-side plan built from the routing description.
@@ -101,6 +103,14 @@ void timing_end(int kind, cudaStream_t st, cudaEvent_t (&ev)[2]);
 __device__ int g_err_word = 0;
 constexpr int kErrBounds = 1;
 constexpr int kErrTimeout = 2;
+
+// Record a device-side check in the call's own status word when it has one,
+// else in the library-wide word.
+__device__ __forceinline__ void flag_error(int* err, int bits) { atomicOr(err ? err : &g_err_word, bits); }
+
+// Alignment of a caller pointer (nullptr counts as aligned: it is checked
+// for presence elsewhere).
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // element conversion
 template <class T> __device__ __forceinline__ float to_f(T v);

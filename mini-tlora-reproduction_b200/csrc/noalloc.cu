@@ -23,7 +23,9 @@
 //    the caller;
 //  * the first call on each device resolves the array's device address with
 //    cudaGetSymbolAddress (the host-side name is only a stand-in); make that
-//    first call before any stream capture on that device.
+//    first call before any stream capture on that device.  The address is
+//    cached for the life of the process and is stale after a cudaDeviceReset
+//    of that device.
 #include <mutex>
 
 #include "common.cuh"

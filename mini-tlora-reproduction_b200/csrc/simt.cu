@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(NT) k_main(PlanDev plan, const T* __restrict__
     if (row >= M) continue;
     const int64_t orow = out_rows ? int64_t(out_rows[row]) : row;  // caller's row order
     if (orow < 0 || orow >= M) {  // out_rows is not a permutation of the rows
-      atomicOr(&g_err_word, kErrBounds);
+      flag_error(plan.err, kErrBounds);
       continue;
     }
 #pragma unroll

@@ -176,7 +176,7 @@ __device__ __forceinline__ bool mbar_try_cluster(uint32_t b, uint32_t parity) {
 }
 // Bounded wait.  Returns false if the CTA is aborting or the wait timed out
 // (then the CTA is flagged to abort and the device error word is set).
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
   const uint32_t a = su32(b);
   if (mbar_try(a, parity)) return true;
   const unsigned long long t0 = now_ns();
@@ -186,14 +186,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
       if (*abort_flag) return false;
       if (now_ns() - t0 > kTimeoutNs) {
         *abort_flag = 1;
-        atomicOr(&g_err_word, kErrTimeout);
+        flag_error(err, kErrTimeout);
         return false;
       }
     }
   }
 }
 // bounded wait with cluster-scope acquire (see mbar_try_cluster)
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                                  int* err) {
   const uint32_t a = su32(b);
   if (mbar_try_cluster(a, parity)) return true;
   const unsigned long long t0 = now_ns();
@@ -203,7 +204,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, 
       if (*abort_flag) return false;
       if (now_ns() - t0 > kTimeoutNs) {
         *abort_flag = 1;
-        atomicOr(&g_err_word, kErrTimeout);
+        flag_error(err, kErrTimeout);
         return false;
       }
     }
@@ -473,7 +474,7 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
     }
   }
   if (bad) {
-    atomicOr(&g_err_word, kErrBounds);
+    flag_error(p.plan.err, kErrBounds);
     it.skip = true;
   }
   return it;
@@ -485,7 +486,7 @@ __device__ __forceinline__ Item decode(const TcParams& p, int item, int units) {
 __device__ __forceinline__ int4 reduce_entry(const TcParams& p, int e) {
   int4 d = p.plan.list_desc[e];
   if (d.x < 0 || d.x >= p.plan.n_chunks || d.y < 0 || d.y >= p.plan.n_tiles || d.z < 0 || d.w > 4 || d.z > d.w) {
-    atomicOr(&g_err_word, kErrBounds);
+    flag_error(p.plan.err, kErrBounds);
     d = make_int4(0, 0, 0, 0);
   }
   return d;
@@ -517,8 +518,8 @@ constexpr int kClaimAhead = 8;
 // producer: publish the claimed item (claiming now if none is claimed yet,
 // claimed == -2) in this CTA's ring
 __device__ __forceinline__ bool sched_next(SchedQ& s, int* counter, int n_items, volatile int* abort_flag,
-                                           int& claimed, int& item) {
-  if (!mbar_wait(&s.empty[s.q], s.ph ^ 1, abort_flag)) return false;
+                                           int* err, int& claimed, int& item) {
+  if (!mbar_wait(&s.empty[s.q], s.ph ^ 1, abort_flag, err)) return false;
   const int i = claimed == -2 ? atomicAdd(counter, 1) : claimed;
   claimed = -2;
   item = i < n_items ? i : -1;
@@ -529,8 +530,9 @@ __device__ __forceinline__ bool sched_next(SchedQ& s, int* counter, int n_items,
 }
 // consumer: wait for the next published item (cluster-scope acquire when the
 // item was published by the other CTA of a pair)
-__device__ __forceinline__ bool sched_take(SchedQ& s, bool remote, volatile int* abort_flag, int& item) {
-  if (!(remote ? mbar_wait_cluster(&s.full[s.q], s.ph, abort_flag) : mbar_wait(&s.full[s.q], s.ph, abort_flag)))
+__device__ __forceinline__ bool sched_take(SchedQ& s, bool remote, volatile int* abort_flag, int* err, int& item) {
+  if (!(remote ? mbar_wait_cluster(&s.full[s.q], s.ph, abort_flag, err)
+               : mbar_wait(&s.full[s.q], s.ph, abort_flag, err)))
     return false;
   item = s.item[s.q];
   return true;
@@ -636,7 +638,7 @@ __device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0
     // the row the caller's order puts it in (64 contiguous bytes)
     const int64_t row = row_w0 + lane;
     const int64_t orow = row < p.M ? int64_t(p.out_rows[row]) : -1;
-    if (row < p.M && (orow < 0 || orow >= p.M)) atomicOr(&g_err_word, kErrBounds);  // not a permutation
+    if (row < p.M && (orow < 0 || orow >= p.M)) flag_error(p.plan.err, kErrBounds);  // not a permutation
     if (orow >= 0 && orow < p.M) {
       __nv_bfloat16* dst = p.out + orow * N + n0 + col;
       if (n0 + col + 32 <= N) {
@@ -734,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     int claimed = -2;
     for (int item = 0; ok;) {
-      if (!sched_next(sq, p.counter, p.n_items, abort_flag, claimed, item)) { ok = false; break; }
+      if (!sched_next(sq, p.counter, p.n_items, abort_flag, p.plan.err, claimed, item)) { ok = false; break; }
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
@@ -754,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
 
       for (int kb = 0; kb < it.nk; ++kb) {
         if (kb == claim_kb) claimed = atomicAdd(p.counter, 1);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         uint8_t* sA = smem + stage * stage_bytes;
         uint8_t* sB = sA + kA1Bytes;
         uint64_t* bar = &full[stage];
@@ -836,18 +838,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     for (int item = 0; ok;) {
-      if (!sched_take(sq, false, abort_flag, item)) { ok = false; break; }
+      if (!sched_take(sq, false, abort_flag, p.plan.err, item)) { ok = false; break; }
       mbar_arrive(&sq.empty[sq.q]);
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
-      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(acc * kAccCols);
       const uint32_t idesc = idesc_16(128, it.n, A_MN, B_MN, p.f16 != 0);
       for (int kb = 0; kb < it.nk; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.plan.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sA = su32(smem + stage * stage_bytes);
         const uint64_t ad = sdesc(sA, a_lbo, 1024);
@@ -867,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     tc_commit(drain);
     const unsigned long long t0 = now_ns();
     while (!mbar_try(su32(drain), 0)) {
-      if (now_ns() - t0 > kTimeoutNs) { atomicOr(&g_err_word, kErrTimeout); break; }
+      if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
     }
   } else if (warp >= 2) {
     // ---------------------------------------------------------------- epilogue
@@ -878,14 +880,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     uint32_t acc_phase = 0;
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     for (int item = 0;;) {
-      if (!sched_take(sq, false, abort_flag, item)) break;
+      if (!sched_take(sq, false, abort_flag, p.plan.err, item)) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sq.empty[sq.q]);
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.plan.err)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);
       uint32_t v[32];
@@ -1034,7 +1036,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     for (int item = 0; ok;) {
       if (leader) {
         // publish the claimed item (claim one now if none) to both CTAs
-        if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         const int i = claimed == -2 ? atomicAdd(p.counter, 1) : claimed;
         claimed = -2;
         item = i < p.n_items ? i : -1;
@@ -1043,7 +1045,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
         mbar_arrive(&sq.full[sq.q]);
         mbar_arrive_cluster(peer_full0 + 8u * uint32_t(sq.q));
       } else {
-        if (!sched_take(sq, true, abort_flag, item)) { ok = false; break; }
+        if (!sched_take(sq, true, abort_flag, p.plan.err, item)) { ok = false; break; }
         mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
       }
       sq.advance();
@@ -1055,7 +1057,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
       for (int kb = 0; kb < it.nk; ++kb) {
         if (leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         uint8_t* sA = smem + stage * kStage2Bytes;
         uint8_t* sB = sA + kA2Bytes;
         const uint32_t bar = mapa(su32(&full[stage]), 0);  // the even CTA's barrier
@@ -1109,17 +1111,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     const uint32_t idesc = idesc_16(256, 256, false, B_MN, p.f16 != 0);
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     for (int item = 0; ok;) {
-      if (!sched_take(sq, false, abort_flag, item)) { ok = false; break; }
+      if (!sched_take(sq, false, abort_flag, p.plan.err, item)) { ok = false; break; }
       mbar_arrive(&sq.empty[sq.q]);
       sq.advance();
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
       if (it.skip) continue;
-      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + uint32_t(acc * kAccCols);
       for (int kb = 0; kb < it.nk; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.plan.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sA = su32(smem + stage * kStage2Bytes);
         const uint64_t ad = sdesc(sA, 16u, 1024);
@@ -1138,7 +1140,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     tc_commit_pair_local(drain);
     const unsigned long long t0 = now_ns();
     while (!mbar_try(su32(drain), 0)) {
-      if (now_ns() - t0 > kTimeoutNs) { atomicOr(&g_err_word, kErrTimeout); break; }
+      if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
     }
   } else if (warp >= 2) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
@@ -1151,7 +1153,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     const uint32_t even_empty0 = mapa(su32(sched_empty), 0);
     for (int item = 0;;) {
-      if (!sched_take(sq, !leader, abort_flag, item)) break;
+      if (!sched_take(sq, !leader, abort_flag, p.plan.err, item)) break;
       __syncwarp();
       if (lane == 0) {
         if (leader) mbar_arrive(&sq.empty[sq.q]);
@@ -1161,7 +1163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, 1);
       if (it.skip) continue;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.plan.err)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(acc * kAccCols);
       const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;

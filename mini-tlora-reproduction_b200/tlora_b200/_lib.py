@@ -61,6 +61,7 @@ class Problem(ctypes.Structure):
         ("impl", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
         ("flags", ctypes.c_int32),
+        ("err_word", ctypes.c_void_p),  # device int32 of this call's flags, or NULL (library-wide word)
     ]
 
 
@@ -93,6 +94,7 @@ class PeerAr(ctypes.Structure):
         ("y", ctypes.c_void_p * AR_MAX_RANKS),
         ("done", ctypes.c_void_p * AR_MAX_RANKS),
         ("timeout_ns", ctypes.c_int64),
+        ("err_word", ctypes.c_void_p),
     ]
 
 

@@ -208,8 +208,15 @@ class _CallArgs:
     """Keeps the numpy arrays behind the ctypes structs alive for one call."""
 
     def __init__(self, rows, d_in, d_out, dtype, impl, plan: RoutePlan, table: AdapterTable,
-                 scaling: np.ndarray, max_ctas: int = 0, out_rows: Optional[torch.Tensor] = None, flags: int = 0):
-        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas), int(flags))
+                 scaling: np.ndarray, max_ctas: int = 0, out_rows: Optional[torch.Tensor] = None, flags: int = 0,
+                 err_word: Optional[torch.Tensor] = None):
+        # err_word: a device int32 tensor that receives this call's device-side
+        # flags (bounds bit 0, timeout bit 1) instead of the library-wide word
+        if err_word is not None and (err_word.dtype != torch.int32 or err_word.device.type != "cuda"):
+            raise ValueError("err_word must be a CUDA int32 tensor")
+        self.prob = _lib.Problem(rows, d_in, d_out, dtype, _IMPLS[impl], int(max_ctas), int(flags),
+                                 err_word.data_ptr() if err_word is not None else None)
+        self.err_word = err_word  # kept alive for the call
         self.seg_start = np.ascontiguousarray(plan.seg_start, dtype=np.int32)
         self.seg_adapter = np.ascontiguousarray(plan.seg_adapter, dtype=np.int32)
         self.rank = np.ascontiguousarray(table.rank, dtype=np.int32)
@@ -240,6 +247,9 @@ class LayerState:
     B_pack: torch.Tensor
     impl: str = "auto"
     max_ctas: int = 0  # cap on persistent-kernel CTAs (0 = one per SM)
+    # device int32 tensor that receives the device-side flags of the calls made
+    # with this state (bounds bit 0, timeout bit 1); None = the library-wide word
+    err_word: Optional[torch.Tensor] = None
 
 
 def _resident_key(rows, d_in, d_out, dtype, st: LayerState):
@@ -284,7 +294,7 @@ def forward_raw(x, W, bias, st: LayerState, x_sorted=None):
     d_out = st.B_pack.shape[0]
     xs = x_sorted if x_sorted is not None else (gather_rows(x, st.plan.perm) if st.plan.perm is not None else x)
     args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling,
-                     out_rows=st.plan.perm)
+                     out_rows=st.plan.perm, err_word=st.err_word)
     zb, wb = args.sizes()
     dev = x.device
     y = torch.empty(rows, d_out, dtype=x.dtype, device=dev)
@@ -307,7 +317,7 @@ class StagedForward:
         rows, d_in = x.shape
         d_out = st.B_pack.shape[0]
         self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(x.dtype), st.impl, st.plan, st.table, st.scaling,
-                              st.max_ctas)
+                              st.max_ctas, err_word=st.err_word)
         zb, wb = self.args.sizes()
         dev = x.device
         self.y = y if y is not None else torch.empty(rows, d_out, dtype=x.dtype, device=dev)
@@ -358,7 +368,7 @@ def backward_raw(dy, xs, W, z, st: LayerState, want_dx: bool, want_dA: bool, wan
     dev = dy.device
     dys = gather_rows(dy, st.plan.perm) if st.plan.perm is not None else dy
     args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
-                     out_rows=st.plan.perm)
+                     out_rows=st.plan.perm, err_word=st.err_word)
     _, wb = args.sizes()
     ws, args.prob.flags = _workspace(st, args, wb, dev)
     dx = torch.empty(rows, d_in, dtype=dy.dtype, device=dev) if want_dx else None
@@ -387,7 +397,7 @@ class StagedBackward:
         d_out = st.B_pack.shape[0]
         dev = dy.device
         self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
-                              st.max_ctas)
+                              st.max_ctas, err_word=st.err_word)
         zb, wb = self.args.sizes()
         self.ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
         self.wb = wb

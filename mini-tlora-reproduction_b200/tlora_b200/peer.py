@@ -132,6 +132,14 @@ class PeerAllReduce:
                 a.link(b.rank, b.base)
         return ranks
 
+    def set_err_word(self, err_word: Optional[torch.Tensor]) -> None:
+        """Report this rank's timeouts into ``err_word`` (a device int32
+        tensor kept alive by this object) instead of the library-wide word."""
+        if err_word is not None and (err_word.dtype != torch.int32 or err_word.device != self.device):
+            raise ValueError("err_word must be an int32 tensor on this rank's device")
+        self._err_word = err_word
+        self.ar.err_word = err_word.data_ptr() if err_word is not None else None
+
     # -- calls ---------------------------------------------------------------
     def reset(self, stream=None) -> None:
         """Zero this rank's counters (before the ranks' barrier of a call)."""

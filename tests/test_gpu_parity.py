@@ -389,6 +389,44 @@ def test_out_rows_outside_the_rows_sets_the_bounds_flag():
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("impl", ["tc", "simt"])
+def test_per_call_error_words_on_two_streams(impl):
+    """Two calls running at the same time on two streams, each with its own
+    status word (mlora_problem.err_word): the call whose out_rows has an entry
+    outside the rows flags bit 0 in its own word only; the other call's word
+    and the library-wide word stay zero, and the good call's Y is complete."""
+    from tlora_b200 import ops, _lib
+    dtype = torch.bfloat16
+    m = _edge_module(256, 200, {0: 8}, dtype)
+    ids = torch.zeros(300, dtype=torch.int64, device=DEV)
+    x = torch.randn(300, 256, device=DEV).to(dtype)
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(ids, table, torch.device(DEV))
+    bad = torch.arange(300, dtype=torch.int32, device=DEV)
+    bad[7] = 300
+    good = torch.arange(300, dtype=torch.int32, device=DEV)
+    words = [torch.zeros(1, dtype=torch.int32, device=DEV) for _ in range(2)]
+    sts = [ops.LayerState(table, np.array([1.5], np.float32),
+                          ops.RoutePlan(300, plan.seg_start, plan.seg_adapter, perm, plan.active), A_pack, B_pack,
+                          impl, err_word=wd) for perm, wd in ((bad, words[0]), (good, words[1]))]
+    _lib.clear_device_error()
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    ys = []
+    for st, s in zip(sts, streams):
+        with torch.cuda.stream(s):
+            ys.append(ops.forward_raw(x, m.base.weight, m.base.bias, st, x_sorted=x)[0])
+    torch.cuda.synchronize()
+    assert int(words[0].item()) & 1
+    assert int(words[1].item()) == 0
+    assert _lib.device_error() == 0
+    y_ref, _, _, _ = ops.forward_raw(x, m.base.weight, m.base.bias,
+                                     ops.LayerState(table, np.array([1.5], np.float32), plan, A_pack, B_pack, impl),
+                                     x_sorted=x)
+    torch.cuda.synchronize()
+    assert torch.equal(ys[1], y_ref)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_gather_scatter_rows_round_trip(dtype):
     """mlora_gather_rows / mlora_scatter_rows (the C ABI's row permutation for

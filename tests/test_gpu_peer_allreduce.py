@@ -136,6 +136,32 @@ def test_wait_without_pushes_times_out():
     torch.ones(4, device=DEV).sum().item()  # the device still answers
 
 
+def test_timeout_is_one_deadline_per_launch():
+    """Nothing pushes and every finisher warp holds many work units (about
+    ten): the launch still returns after about one timeout, because all the
+    waits of a launch share one deadline; the flag lands in this rank's own
+    status word (mlora_peer_ar.err_word), not in the library-wide word."""
+    import time
+    _lib.clear_device_error()
+    rows = 2 * 740 * 256  # 1480 tiles: rank 0 owns 740 x 32 work units, ~10 per warp at 148 x 16 warps
+    timeout_s = 0.05
+    ars = peer.PeerAllReduce.emulated(2, rows, 256, torch.bfloat16, DEV, timeout_s=timeout_s)
+    word = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ars[0].set_err_word(word)
+    for a in ars:
+        a.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ars[0].finish(0, ars[0].n_tiles)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert int(word.item()) & 2
+    assert _lib.device_error() == 0
+    for a in ars:
+        a.close()
+    assert elapsed < 4 * timeout_s, f"finish took {elapsed:.3f} s with a {timeout_s} s timeout"
+
+
 def test_push_argument_checks():
     w = workloads.build(_ragged_spec(), device=DEV)
     L = ShardedLayer(w.model, 0, 1, compute=NativeCompute("tc"))

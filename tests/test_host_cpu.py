@@ -52,6 +52,38 @@ def test_status_strings_and_sizes_without_gpu():
         ops._CallArgs(300, 256, 128, _lib.BF16, "auto", bad, table, np.ones(3, np.float32)).sizes()
 
 
+def test_misaligned_pointers_rejected_before_any_launch():
+    """The tensor-core kernels read every tensor with TMA or 16-byte vector
+    accesses: an explicit tensor-core call given a pointer that is not 16-byte
+    aligned (here a bias slice 2 bytes in) returns MLORA_ERR_UNSUPPORTED before
+    any CUDA call, and a pointer not aligned to its element size is rejected on
+    every kernel family.  Fake device addresses: nothing is dereferenced."""
+    import ctypes
+
+    lib = _lib.lib()
+    table = ops.AdapterTable.build([0, 1], [8, 64])
+    plan = ops.RoutePlan(300, np.array([0, 100, 300], np.int32), np.array([0, 1], np.int32))
+    base = 1 << 40  # 16-byte aligned fake device addresses
+    P = [ctypes.c_void_p(base + i * (1 << 30)) for i in range(8)]
+
+    def fwd(impl, bias, x=P[0]):
+        args = ops._CallArgs(300, 256, 128, _lib.BF16, impl, plan, table, np.ones(2, np.float32))
+        zb, wb = args.sizes()
+        return lib.mlora_forward(ctypes.byref(args.prob), ctypes.byref(args.route), x, P[1], bias, P[2], P[3],
+                                 P[4], P[5], P[6], wb, None)
+
+    for impl in ("tc", "tc1", "tc2"):
+        assert fwd(impl, ctypes.c_void_p(base + 2)) == _lib.ERR_UNSUPPORTED  # bias 2 bytes in
+        assert fwd(impl, P[7], x=ctypes.c_void_p(base + 8)) == _lib.ERR_UNSUPPORTED
+    for impl in ("tc", "simt", "auto"):  # odd address: not even element-aligned
+        assert fwd(impl, ctypes.c_void_p(base + 1)) == _lib.ERR_UNSUPPORTED
+
+    args = ops._CallArgs(300, 256, 128, _lib.BF16, "tc", plan, table, np.ones(2, np.float32))
+    _, wb = args.sizes()
+    assert lib.mlora_backward(ctypes.byref(args.prob), ctypes.byref(args.route), P[0], P[1], P[2], P[3], P[4],
+                              P[5], P[6], P[7], ctypes.c_void_p(base + 4), P[1], wb, None) == _lib.ERR_UNSUPPORTED
+
+
 def test_peer_allreduce_layout_and_checks_without_gpu():
     """Receive-buffer and counter sizes of the peer all-reduce (host
     arithmetic), and the argument checks that run before any CUDA call."""
