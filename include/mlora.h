@@ -228,6 +228,46 @@ int mlora_ar_finish(const mlora_peer_ar* ar, int64_t rows, int32_t dtype, int32_
 /* Wait until every tile of this rank's Y holds the sum. */
 int mlora_ar_wait(const mlora_peer_ar* ar, void* stream);
 
+/* ---- Partial-Y all-reduce of the K-sharded forward through the NVSwitch
+ * (multimem; replaces the SUM all-reduce of each nano-batch's Y rows,
+ * phase6_two_gpu_overlap.py:247-280).
+ *
+ * Every rank's Y [rows, d_out] and flag words (MLORA_MC_FLAG_WORDS uint32,
+ * zero before the first use) sit at the same offsets of buffers bound to one
+ * NVLink multicast object (e.g. torch symmetric memory); y_mc / flags_mc are
+ * the multicast addresses, flags this rank's own copy.  After the rank's
+ * forward mainloop of a nano-batch has written its partial rows (stream
+ * order), mlora_mc_allreduce(rows [row_begin, row_end), slot, use) tells every
+ * rank that this rank's partial rows are in place, waits (bounded) until all
+ * ranks have said so, and sums this rank's 1/world share of the rows in place
+ * with multimem.ld_reduce (fp32 accumulation in the switch, one rounding) and
+ * multimem.st (the sum lands in every rank's Y).  `slot` identifies the
+ * nano-batch within a step (< MLORA_MC_SLOTS) and `use` counts this slot's
+ * uses, 1, 2, ... (the same on every rank).  mlora_mc_wait(n_slots, uses)
+ * waits (bounded) until every rank has written its sums of slots
+ * [0, n_slots) into this rank's Y; the caller's stream must wait for it
+ * before Y is read or the next forward rewrites it.  Every wait of a launch
+ * gives up at one deadline (timeout_ns, 0 = 2 s), sets the timeout bit of
+ * err_word (or of the library-wide word) and lets the launch finish.
+ * Requires 16-bit dtypes and d_out % 8 == 0.  No counterpart beyond the
+ * reference's all-reduce. */
+#define MLORA_MC_SLOTS 64
+#define MLORA_MC_FLAG_WORDS (3 * MLORA_MC_SLOTS)
+typedef struct mlora_mc_ar {
+  int32_t rank, world;
+  int64_t rows;          /* rows of Y */
+  int32_t d_out;         /* columns of Y */
+  int32_t dtype;         /* MLORA_BF16 or MLORA_F16 */
+  void* y_mc;            /* multicast address of Y */
+  uint32_t* flags_mc;    /* multicast address of the flag words */
+  uint32_t* flags;       /* this rank's flag words */
+  int64_t timeout_ns;
+  int32_t* err_word;     /* optional DEVICE int32 for this rank's flags; NULL = library-wide word */
+} mlora_mc_ar;
+int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int64_t row_end, int32_t slot, uint32_t use,
+                       void* stream);
+int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, const uint32_t* uses, void* stream);
+
 /* Peer memory for the buffers above: one cudaMalloc'd block per rank, shared
  * with the other processes by CUDA IPC (64-byte handles). */
 int mlora_peer_alloc(size_t bytes, void** ptr);

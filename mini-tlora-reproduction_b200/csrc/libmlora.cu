@@ -7,5 +7,6 @@
 #include "route.cu"
 #include "tc.cu"
 #include "allreduce.cu"
+#include "multimem.cu"
 #include "api.cu"
 #include "noalloc.cu"

@@ -98,6 +98,26 @@ class PeerAr(ctypes.Structure):
     ]
 
 
+MC_SLOTS = 64
+MC_FLAG_WORDS = 3 * MC_SLOTS
+
+
+class McAr(ctypes.Structure):
+    """mlora_mc_ar: the multicast buffers of the K-sharded forward's all-reduce."""
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("rows", ctypes.c_int64),
+        ("d_out", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("y_mc", ctypes.c_void_p),
+        ("flags_mc", ctypes.c_void_p),
+        ("flags", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_int64),
+        ("err_word", ctypes.c_void_p),
+    ]
+
+
 class SgdItem(ctypes.Structure):
     _fields_ = [
         ("param", ctypes.c_void_p),
@@ -130,6 +150,9 @@ SIGNATURES = {
     "mlora_ar_finish": (ctypes.c_int, [ctypes.POINTER(PeerAr), ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _VP]),
     "mlora_ar_wait": (ctypes.c_int, [ctypes.POINTER(PeerAr), _VP]),
+    "mlora_mc_allreduce": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                          ctypes.c_uint32, _VP]),
+    "mlora_mc_wait": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32), _VP]),
     "mlora_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "mlora_peer_free": (ctypes.c_int, [_VP]),
     "mlora_ipc_handle": (ctypes.c_int, [_VP, _VP]),

@@ -322,9 +322,15 @@ class StagedForward:
         dev = x.device
         self.y = y if y is not None else torch.empty(rows, d_out, dtype=x.dtype, device=dev)
         self.z = torch.empty(max(zb, 1), dtype=torch.uint8, device=dev)
-        self.ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+        # the plan's resident workspace when make_resident() uploaded one for
+        # this shape: the calls then copy nothing from the host
+        self.ws, self.args.prob.flags = _workspace(st, self.args, wb, dev)
         self.wb = wb
         self.n_tiles = int(_lib.lib().mlora_num_tiles(rows))
+
+    def rebind(self, x) -> None:
+        """Reuse this object for another call with the same plan and shapes."""
+        self.x = x
 
     def _run(self, stages, t0, t1, bias):
         _lib.call("mlora_forward_staged", ctypes.byref(self.args.prob), ctypes.byref(self.args.route),
@@ -333,6 +339,12 @@ class StagedForward:
 
     def shrink(self, t0=0, t1=None):
         self._run(_lib.STAGE_SHRINK, t0, self.n_tiles if t1 is None else t1, None)
+
+    def shrink_main(self, expand=True, add_bias=True):
+        """Shrink and mainloop over all tiles in one call: the mainloop is
+        launched to overlap the shrink's tail (programmatic dependent launch)."""
+        stages = _lib.STAGE_SHRINK | _lib.STAGE_MAIN | (0 if expand else _lib.STAGE_NO_EXPAND)
+        self._run(stages, 0, self.n_tiles, self.bias if add_bias else None)
 
     def main(self, t0=0, t1=None, expand=True, add_bias=True, max_ctas=None):
         """``max_ctas`` (default: the state's) caps the mainloop's CTAs for
@@ -399,7 +411,7 @@ class StagedBackward:
         self.args = _CallArgs(rows, d_in, d_out, mlora_dtype(dy.dtype), st.impl, st.plan, st.table, st.scaling,
                               st.max_ctas, err_word=st.err_word)
         zb, wb = self.args.sizes()
-        self.ws = torch.empty(max(wb, 1), dtype=torch.uint8, device=dev)
+        self.ws, self.args.prob.flags = _workspace(st, self.args, wb, dev)
         self.wb = wb
         self.dz_bytes = zb
         self.dz = torch.zeros(max(zb, 1), dtype=torch.uint8, device=dev)
@@ -408,6 +420,17 @@ class StagedBackward:
         self.dB = torch.zeros_like(st.B_pack)
         self.n_tiles = int(_lib.lib().mlora_num_tiles(rows))
         self.n_db = (d_out + 127) // 128
+
+    def rebind(self, dy, xs, z) -> None:
+        """Reuse this object (its buffers and call arguments) for another call
+        with the same plan and shapes: new dY, X and saved intermediate."""
+        self.dy, self.xs, self.z = dy, xs, z
+
+    def zero_partials(self) -> None:
+        """Zero dZ and dB before a call that writes only some of their blocks
+        (a K-sharded rank's share), so that the ranks' buffers can be summed."""
+        self.dz.zero_()
+        self.dB.zero_()
 
     def dz_view(self):
         return self.dz[:self.dz_bytes].view(self.dy.dtype) if self.dz_bytes else None
@@ -429,6 +452,15 @@ class StagedBackward:
 
     def run_db(self, b0=0, b1=None):
         self._run(_lib.BWD_DB, 0, 0, b0, self.n_db if b1 is None else b1)
+
+    def run_all(self):
+        """Every stage over all tiles in one call (dZ, then the dX mainloop
+        overlapping its tail, then dA and dB in one reduction launch)."""
+        self._run(_lib.BWD_DZ | _lib.BWD_DX | _lib.BWD_DA | _lib.BWD_DB, 0, self.n_tiles, 0, self.n_db)
+
+    def run_dadb(self, b0=0, b1=None):
+        """dA and dB (d_out blocks [b0, b1)) in one reduction launch."""
+        self._run(_lib.BWD_DA | _lib.BWD_DB, 0, 0, b0, self.n_db if b1 is None else b1)
 
 
 class MultiLoRAFunction(torch.autograd.Function):

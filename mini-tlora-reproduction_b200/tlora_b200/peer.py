@@ -167,3 +167,88 @@ class PeerAllReduce:
         if self.base:
             _lib.call("mlora_peer_free", ctypes.c_void_p(self.base))
             self.base = 0
+
+
+class MulticastAllReduce:
+    """One rank's buffers of the all-reduce through the NVSwitch's multicast
+    objects (``mlora_mc_allreduce`` / ``mlora_mc_wait``): Y [rows, d_out] and
+    the flag words live in one torch symmetric-memory buffer per rank, bound
+    to an NVLink multicast object by ``rendezvous`` (collective over
+    ``group``).  The mainloop of each nano-batch writes this rank's partial
+    rows into ``y``; ``reduce(r0, r1, slot)`` then sums them across the ranks
+    in place (every rank's ``y`` ends up holding the sum) and ``wait(n)``
+    makes a stream wait until the sums of slots [0, n) are in this rank's
+    ``y``.  ``available(group)`` tells whether the GPUs support multicast."""
+
+    def __init__(self, rows: int, d_out: int, dtype: torch.dtype, device, group=None, timeout_s: float = 2.0):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise NotImplementedError("the multicast all-reduce sums 16-bit values (bf16 or fp16)")
+        if d_out % 8:
+            raise ValueError("d_out must be a multiple of 8")
+        self.rows, self.d_out, self.dtype = int(rows), int(d_out), dtype
+        self.device = torch.device(device)
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        y_bytes = _round(self.rows * self.d_out * 2)
+        self.buf = symm_mem.empty(y_bytes + 4 * _lib.MC_FLAG_WORDS, dtype=torch.uint8, device=self.device)
+        self.buf[y_bytes:].zero_()  # the flag words start at zero on every rank
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        mc = int(self.handle.multicast_ptr)
+        if not mc:
+            raise RuntimeError("these GPUs expose no NVLink multicast object (no NVSwitch multicast support)")
+        local = int(self.handle.buffer_ptrs[self.rank])
+        off = self.buf.data_ptr() - local  # the tensor's offset inside the symmetric allocation
+        if off < 0 or off + self.buf.numel() > int(self.handle.buffer_size):
+            raise RuntimeError("the symmetric buffer does not cover the tensor: no multicast address for it")
+        self.y = self.buf[:self.rows * self.d_out * 2].view(dtype).view(self.rows, self.d_out)
+        self.ar = _lib.McAr()
+        self.ar.rank, self.ar.world, self.ar.rows, self.ar.d_out = self.rank, self.world, self.rows, self.d_out
+        self.ar.dtype = _lib.F16 if dtype == torch.float16 else _lib.BF16
+        self.ar.y_mc = mc + off
+        self.ar.flags_mc = mc + off + y_bytes
+        self.ar.flags = self.buf.data_ptr() + y_bytes
+        self.ar.timeout_ns = int(timeout_s * 1e9)
+        self.uses = [0] * _lib.MC_SLOTS
+        self._err_word = None
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every rank's flags are zero before any rank signals
+
+    @staticmethod
+    def available() -> bool:
+        """True when torch's symmetric memory can be imported (whether the GPUs
+        support multicast is known only after the collective rendezvous)."""
+        try:
+            import torch.distributed._symmetric_memory  # noqa: F401
+            return True
+        except Exception:
+            return False
+
+    def set_err_word(self, err_word: Optional[torch.Tensor]) -> None:
+        if err_word is not None and (err_word.dtype != torch.int32 or err_word.device != self.device):
+            raise ValueError("err_word must be an int32 tensor on this rank's device")
+        self._err_word = err_word
+        self.ar.err_word = err_word.data_ptr() if err_word is not None else None
+
+    def reduce(self, r0: int, r1: int, slot: int, stream=None) -> None:
+        """Sum rows [r0, r1) of ``y`` across the ranks, in place, as nano-batch
+        ``slot`` of the step (after this rank's partial rows are written, in
+        the order of ``stream``)."""
+        self.uses[slot] += 1
+        _lib.call("mlora_mc_allreduce", ctypes.byref(self.ar), int(r0), int(r1), int(slot), self.uses[slot],
+                  _stream_handle(stream, self.device))
+
+    def wait(self, n_slots: int, stream=None) -> None:
+        """``stream`` waits until every rank's sums of slots [0, n_slots) are in
+        this rank's ``y``."""
+        uses = (ctypes.c_uint32 * max(1, n_slots))(*self.uses[:n_slots])
+        _lib.call("mlora_mc_wait", ctypes.byref(self.ar), int(n_slots), uses, _stream_handle(stream, self.device))
+
+    def close(self) -> None:
+        """Release the buffer (collective: after every rank's device work)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.handle = None
+        self.buf = None
+        self.y = None

@@ -1,6 +1,7 @@
-"""World-size-2 gloo tests (CPU) of the K-sharded nano-batch pipeline: the
-sharding, the per-nano-batch all-reduce choreography and the rank-0-only
-bias / LoRA expand must reproduce the unsharded layer (the oracle).  The
+"""Multi-rank gloo tests (CPU, world sizes 1-3) of the K-sharded nano-batch
+pipeline: the sharding, the per-nano-batch all-reduce choreography (Z, Y, dZ
+and the async dB all-reduce) and the bias / LoRA expand added by one owner
+rank per nano-batch must reproduce the unsharded layer (the oracle).  The
 native kernels are replaced by a dense torch stand-in with the same stage
 semantics; the kernels themselves are covered by the GPU parity tests."""
 
@@ -58,7 +59,7 @@ class DenseCompute:
             v = v + L.bias
         ctx["y"][r0:r1] = v
 
-    def bwd_begin(self, ctx, layer, x_p, dy, overlapped=False):
+    def bwd_begin(self, ctx, layer, x_p, dy, overlapped=False, partial=True):
         rows = x_p.shape[0]
         d_out = layer.B_pack.shape[0]
         return {"ctx": ctx, "layer": layer, "x": x_p, "dy": dy,
@@ -71,14 +72,20 @@ class DenseCompute:
         r0, r1 = t0 * TILE, min(t1 * TILE, b["x"].shape[0])
         b["dz"][r0:r1] = (b["dy"][r0:r1] @ L.B_pack) * ctx["mask"][r0:r1]
 
-    def bwd_dx_da(self, b):
+    def bwd_dx(self, b):
         L = b["layer"]
         b["dx"] = b["dy"] @ L.W + b["dz"] @ L.A_pack
+
+    def bwd_da(self, b):
         b["dA"] = b["dz"].T @ b["x"]
 
     def bwd_db(self, b, b0, b1):
         r0, r1 = b0 * 128, min(b1 * 128, b["dB"].shape[0])
         b["dB"][r0:r1] = b["dy"][:, r0:r1].T @ b["ctx"]["z"]
+
+    def bwd_dadb(self, b):
+        self.bwd_da(b)
+        self.bwd_db(b, 0, b["n_db"])
 
     def sgd(self, layer, plan, dA, dB, lr):
         for i in range(layer.table.n):
@@ -116,15 +123,15 @@ def _worker(rank, world, port, n_nano, pipelined, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         m, ids, x, dy = _build()
-        layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group([0, 1]))
+        layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group(list(range(world))))
         plan = ops.route(ids, layer.table, torch.device("cpu"))
         x_p = layer.shard_input(x)
         y, dx_p = layer.step(x_p, plan, dy, n_nano, lr=0.01, pipelined=pipelined)
-        sizes = [shard_columns(256, r, world) for r in range(world)]
-        parts = [torch.zeros(x.shape[0], e - s, dtype=torch.float64) for s, e in sizes]
-        dist.all_gather(parts, dx_p.contiguous())
-        a_parts = [torch.zeros(layer.A_pack.shape[0], e - s, dtype=torch.float64) for s, e in sizes]
-        dist.all_gather(a_parts, layer.A_pack.contiguous())
+        # shards of unequal width (64-column blocks): gathered as objects
+        parts = [None] * world
+        dist.all_gather_object(parts, dx_p.contiguous())
+        a_parts = [None] * world
+        dist.all_gather_object(a_parts, layer.A_pack.contiguous())
         if rank == 0:
             q.put({"y": y.numpy().copy(), "dx": torch.cat(parts, 1).numpy(),
                    "A_pack": torch.cat(a_parts, 1).numpy(), "B_pack": layer.B_pack.numpy().copy(),
@@ -133,9 +140,9 @@ def _worker(rank, world, port, n_nano, pipelined, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n_nano,pipelined", [(1, True), (3, True), (2, False), (16, True)])
-def test_sharded_step_matches_unsharded(n_nano, pipelined):
-    world = 2
+@pytest.mark.parametrize("world,n_nano,pipelined", [(2, 1, True), (2, 3, True), (2, 2, False), (3, 4, True),
+                                                    (1, 2, True)])
+def test_sharded_step_matches_unsharded(world, n_nano, pipelined):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
