@@ -236,8 +236,10 @@ class ShardedLayer:
         d_in = model.base.in_features
         self.k0, self.k1 = shard_columns(d_in, rank, world)
         with torch.no_grad():
-            self.W = model.base.weight[:, self.k0:self.k1].contiguous()
-            self.A_pack = A_pack[:, self.k0:self.k1].contiguous()
+            # copies (also with one rank, where the slice is the whole tensor):
+            # the layer's SGD steps update its own adapter shards, not the model's
+            self.W = model.base.weight[:, self.k0:self.k1].clone(memory_format=torch.contiguous_format)
+            self.A_pack = A_pack[:, self.k0:self.k1].clone(memory_format=torch.contiguous_format)
             self.B_pack = B_pack.clone()
             # every rank keeps the bias: the rank that owns a nano-batch adds it
             self.bias = model.base.bias.detach().clone() if model.base.bias is not None else None

@@ -43,6 +43,12 @@ class _DeviceArray:
                                          "version": 3, "strides": None}
 
 
+def _full_device(device) -> torch.device:
+    """``device`` with its index (the current device for a bare "cuda")."""
+    d = torch.device(device)
+    return torch.device(d.type, torch.cuda.current_device()) if d.type == "cuda" and d.index is None else d
+
+
 def _stream_handle(stream: Optional[torch.cuda.Stream], device) -> ctypes.c_void_p:
     s = stream if stream is not None else torch.cuda.current_stream(device)
     return ctypes.c_void_p(s.cuda_stream)
@@ -61,7 +67,7 @@ class PeerAllReduce:
         if not 1 <= world <= _lib.AR_MAX_RANKS or not 0 <= rank < world:
             raise ValueError(f"rank {rank} of {world} ranks (at most {_lib.AR_MAX_RANKS})")
         self.rows, self.d_out, self.dtype, self.rank, self.world = int(rows), int(d_out), dtype, rank, world
-        self.device = torch.device(device)
+        self.device = _full_device(device)
         self.mdtype = _lib.F16 if dtype == torch.float16 else _lib.BF16
         L = _lib.lib()
         self.n_tiles = int(L.mlora_num_tiles(self.rows))
@@ -188,9 +194,15 @@ class MulticastAllReduce:
         if d_out % 8:
             raise ValueError("d_out must be a multiple of 8")
         self.rows, self.d_out, self.dtype = int(rows), int(d_out), dtype
-        self.device = torch.device(device)
+        self.device = _full_device(device)
         self.group = group if group is not None else dist.group.WORLD
         self.rank, self.world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        S = torch._C._distributed_c10d._SymmetricMemory
+        ok = torch.tensor([1 if S.has_multicast_support(torch._C._autograd.DeviceType.CUDA, self.device.index)
+                           else 0], device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)  # every rank decides alike
+        if not int(ok.item()):
+            raise RuntimeError("these GPUs expose no NVLink multicast object (no NVSwitch multicast support)")
         y_bytes = _round(self.rows * self.d_out * 2)
         self.buf = symm_mem.empty(y_bytes + 4 * _lib.MC_FLAG_WORDS, dtype=torch.uint8, device=self.device)
         self.buf[y_bytes:].zero_()  # the flag words start at zero on every rank
@@ -198,10 +210,12 @@ class MulticastAllReduce:
         mc = int(self.handle.multicast_ptr)
         if not mc:
             raise RuntimeError("these GPUs expose no NVLink multicast object (no NVSwitch multicast support)")
+        # the multicast address maps the start of the symmetric allocation:
+        # use it only for a tensor that starts the allocation and fits in it
         local = int(self.handle.buffer_ptrs[self.rank])
-        off = self.buf.data_ptr() - local  # the tensor's offset inside the symmetric allocation
-        if off < 0 or off + self.buf.numel() > int(self.handle.buffer_size):
-            raise RuntimeError("the symmetric buffer does not cover the tensor: no multicast address for it")
+        off = self.buf.data_ptr() - local
+        if off != 0 or int(self.handle.offset) != 0 or self.buf.numel() > int(self.handle.buffer_size):
+            raise RuntimeError("the symmetric allocation does not start at the buffer: no multicast address for it")
         self.y = self.buf[:self.rows * self.d_out * 2].view(dtype).view(self.rows, self.d_out)
         self.ar = _lib.McAr()
         self.ar.rank, self.ar.world, self.ar.rows, self.ar.d_out = self.rank, self.world, self.rows, self.d_out

@@ -110,7 +110,7 @@ class Workload:
     model: MultiLoRALinear
     x: torch.Tensor
     ids: torch.Tensor
-    dy: torch.Tensor  # upstream gradient of Y (the gradient the layer above hands back)
+    dy: torch.Tensor  # upstream gradient of Y (the gradient the layer above hands back), N(0, 1) / rows
 
 
 def build(sp: WorkloadSpec, device="cuda", dtype=None) -> Workload:
@@ -134,6 +134,8 @@ def build(sp: WorkloadSpec, device="cuda", dtype=None) -> Workload:
     dev = torch.device(device)
     gd = torch.Generator(device=dev).manual_seed(sp.seed + 1000)
     x = torch.randn(sp.rows, sp.d_in, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-    dy = torch.randn(sp.rows, sp.d_out, generator=gd, device=dev, dtype=torch.float32).to(dtype)
+    # the upstream gradient of a loss averaged over the rows (N(0, 1) / rows),
+    # so that repeated SGD steps with it stay bounded
+    dy = (torch.randn(sp.rows, sp.d_out, generator=gd, device=dev, dtype=torch.float32) / max(1, sp.rows)).to(dtype)
     ids = torch.cat([torch.full((c,), i, dtype=torch.int64) for i, c in enumerate(sp.counts)]).to(dev)
     return Workload(sp, m, x, ids, dy)
