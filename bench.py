@@ -205,7 +205,7 @@ def module_config(sp):
 
 # ---------------------------------------------------------------- rooflines
 def role_work(sp, zbytes, world=1):
-    """Algorithmic work per launch of each kernel role on one rank (K-shard of
+    """Algorithmic work per step of each kernel role on one rank (K-shard of
     d_in / world): FLOPs for the tensor-bound mainloops, bytes for the rest."""
     M, do = sp.rows, sp.d_out
     di = sp.d_in // world
@@ -219,15 +219,17 @@ def role_work(sp, zbytes, world=1):
         "bwd_shrink": ("hbm", (e * M * do + zbytes) / world + e * rpack * do),
         # one launch (dA and dB) on one GPU; with K-sharding two launches per step, dA over the
         # rank's d_in shard and dB over its share of d_out: their mean per launch
-        "dadb_reduce": ("hbm", e * M * (di + do) + 2 * zbytes + e * rpack * (di + do) if world == 1 else
-                        0.5 * ((e * M * di + zbytes + e * rpack * di) + (e * M * do / world + zbytes +
-                                                                          e * rpack * do / world))),
+        # dA over the rank's d_in shard and dB over its share of d_out (one launch on one GPU)
+        "dadb_reduce": ("hbm", (e * M * di + zbytes + e * rpack * di) + (e * M * do / world + zbytes +
+                                                                         e * rpack * do / world)),
     }
 
 
-def rooflines(sp, kinds, zbytes, peaks_d, peaks_kind, world=1):
-    """Per kernel role: algorithmic work per launch / measured average launch
-    time against the bound that applies.  Tensor-bound roles against the
+def rooflines(sp, kinds, zbytes, peaks_d, peaks_kind, world=1, steps=1):
+    """Per kernel role: algorithmic work per step / the role's measured device
+    time per step (``steps`` steps timed; a role may launch several times a
+    step, e.g. one forward mainloop per nano-batch) against the bound that
+    applies.  Tensor-bound roles against the
     measured burst bf16 GEMM peak (``frac``; the sustained peak of a
     seconds-long GEMM loop under the power cap as ``frac_sustained``); HBM
     roles against the measured copy bandwidth.  `traffic` = DRAM bytes per
@@ -247,7 +249,7 @@ def rooflines(sp, kinds, zbytes, peaks_d, peaks_kind, world=1):
         if k not in work or n <= 0:
             continue
         bound, w = work[k]
-        avg = ms_tot / n
+        avg = ms_tot / steps  # device ms of the role per step
         if bound == "tensor":
             ach = w / (avg / 1000.0) / 1e12
             peak = float(peaks_d.get("bf16_tflops"))
@@ -255,13 +257,13 @@ def rooflines(sp, kinds, zbytes, peaks_d, peaks_kind, world=1):
             out[k] = {"bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
                       "frac": round(ach / peak, 4), "peak_kind": f"{peaks_kind} burst bf16 GEMM",
                       "frac_sustained": round(ach / sus, 4), "algorithmic": w, "traffic": traffic.get(k),
-                      "avg_launch_ms": round(avg, 4)}
+                      "ms_per_step": round(avg, 4), "launches_per_step": round(n / steps, 2)}
         else:
             ach = w / (avg / 1000.0) / 1e9
             peak = float(peaks_d.get("hbm_gbs"))
             out[k] = {"bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                       "frac": round(ach / peak, 4), "peak_kind": f"{peaks_kind} HBM copy", "algorithmic": w,
-                      "traffic": traffic.get(k), "avg_launch_ms": round(avg, 4)}
+                      "traffic": traffic.get(k), "ms_per_step": round(avg, 4), "launches_per_step": round(n / steps, 2)}
     return out
 
 
@@ -293,7 +295,7 @@ def vs_cublas(roofs, cub):
     out = {}
     for role, key in (("fwd_main", "fwd"), ("dx_main", "dx")):
         if role in roofs and key in cub and cub[key]["ms"] > 0:
-            out[role] = round(roofs[role]["avg_launch_ms"] / cub[key]["ms"], 4)
+            out[role] = round(roofs[role]["ms_per_step"] / cub[key]["ms"], 4)
     return out
 
 
@@ -375,9 +377,10 @@ def reference_probes(w, probes):
     return out
 
 
-def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes=8):
+def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes=8, step=None):
     """One K-sharded training step checked against the unsharded layer
-    (fp64): Y and dX on sampled rows (dX gathered from the ranks' shards),
+    (fp64), eager or replayed from a graph (``step``): Y and dX on sampled
+    rows (dX gathered from the ranks' shards),
     the gradients dA and dB through bilinear probes (each rank's partial
     probe of its d_in shard summed across the ranks), and the SGD update
     elementwise on this rank's shards.  Returns max relative L2 per tensor."""
@@ -390,8 +393,12 @@ def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes
         layer.A_pack.copy_(A_full[:, layer.k0:layer.k1])
         layer.B_pack.copy_(B_full)
     A0, B0 = layer.A_pack.clone(), layer.B_pack.clone()
-    y, dx_p = layer.step(x_p, plan, w.dy, n_nano, w.spec.lr)
-    dA_p, dB = layer.last_grads
+    if step is not None:  # a GraphedShardedStep of this layer and inputs
+        y, dx_p = step()
+        dA_p, dB = step.grads
+    else:
+        y, dx_p = layer.step(x_p, plan, w.dy, n_nano, w.spec.lr)
+        dA_p, dB = layer.last_grads
     torch.cuda.synchronize(dev)
     Y_ref, dX_ref = reference_rows(w, rows)
     out = {"Y": _rel(y[rows], Y_ref)}
@@ -473,24 +480,41 @@ def nvlink_roofline(sp, world, ms, comm, peaks_d, link_gbs):
                      "measured in this run)"}
 
 
-def peer_copy_gbs(dev, world, rank, nbytes=256 << 20, iters=5):
-    """Per-direction link bandwidth between ranks, measured now: every rank
-    sends `nbytes` to the next rank and receives from the previous one (NCCL
-    send / recv, all pairs at once), device time, min over ranks."""
+def peer_copy_gbs(dev, world, rank, nbytes=512 << 20, iters=5):
+    """Per-direction link bandwidth between ranks, measured now with this
+    library's plain copy kernel (mlora_peer_copy): every rank writes `nbytes`
+    into the next rank's buffer (a CUDA IPC mapping), all ranks at once, so
+    each GPU sends and receives `nbytes`; device time, max over ranks."""
     if world < 2:
         return None
-    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    rbuf = torch.empty_like(buf)
-    nxt, prv = (rank + 1) % world, (rank - 1) % world
+    import ctypes
+
+    from tlora_b200 import _lib
+    src = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    src.fill_(rank)
+    dst = ctypes.c_void_p(0)
+    _lib.call("mlora_peer_alloc", nbytes, ctypes.byref(dst))
+    h = (ctypes.c_char * 64)()
+    _lib.call("mlora_ipc_handle", dst, h)
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(h))
+    peer = ctypes.c_void_p(0)
+    _lib.call("mlora_ipc_open", (ctypes.c_char * 64).from_buffer_copy(handles[(rank + 1) % world]),
+              ctypes.byref(peer))
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
     def xfer():
-        ops = [dist.P2POp(dist.isend, buf, nxt), dist.P2POp(dist.irecv, rbuf, prv)]
-        for r in dist.batch_isend_irecv(ops):
-            r.wait()
+        _lib.call("mlora_peer_copy", peer, ctypes.c_void_p(src.data_ptr()), nbytes, stream)
 
-    xfer()
-    ms = timed(xfer, iters, dev, world)
-    del buf, rbuf
+    try:
+        xfer()
+        ms = timed(xfer, iters, dev, world)
+    finally:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        _lib.call("mlora_ipc_close", peer)
+        dist.barrier()
+        _lib.call("mlora_peer_free", dst)
     return round(nbytes / (ms / 1e3) / 1e9, 1)
 
 
@@ -507,17 +531,46 @@ def one_timeline(layer, step, dev):
         layer.timeline = None
 
 
+def host_and_device(fn, iters, dev, world):
+    """(device ms per call, host ms per call to enqueue it) over `iters`
+    calls, bracketed as `timed`; both max over ranks.  A host time at the
+    device time means the host's launches set the pace."""
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        fn()
+    host = (time.perf_counter() - t0) * 1e3 / iters
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / iters, host], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0].item()), float(t[1].item())
+
+
 def run_path(layer, w, x_p, plan, comm, args, dev, world):
-    """Time one all-reduce path of the K-sharded step: the nano-batch sweep,
-    AIMD over the real step (phase6b_real_aimd.py:245-302), the timed steps,
-    the overlap accounting, one step's phase timeline and the parity check."""
+    """Time one all-reduce path of the K-sharded step, each step replayed from
+    a CUDA graph (one graph per nano-batch count): the nano-batch sweep, AIMD
+    over the real step (phase6b_real_aimd.py:245-302), the timed steps, the
+    eager step beside it (device and host time), the overlap accounting, one
+    step's phase timeline and the parity check of the graphed step."""
     from tlora_b200 import _lib
     from tlora_b200.nano import AIMDController
-    from tlora_b200.overlap import comm_only
+    from tlora_b200.overlap import GraphedShardedStep, comm_only
 
     layer.comm = comm
     n_tiles = (w.spec.rows + 255) // 256
     lr, dy = w.spec.lr, w.dy
+    graphs = {}
+
+    def graphed(n, comm_on=True):
+        if (n, comm_on) not in graphs:
+            graphs[(n, comm_on)] = GraphedShardedStep(layer, x_p, plan, dy, n, lr, comm=comm_on)
+        return graphs[(n, comm_on)]
 
     def stepper(n, pipelined=True, comm_on=True):
         return lambda: layer.step(x_p, plan, dy, n, lr, pipelined, comm_on)
@@ -526,56 +579,66 @@ def run_path(layer, w, x_p, plan, comm, args, dev, world):
         stepper(1 if world == 1 else 2)()
     torch.cuda.synchronize(dev)
     res = {"allreduce": comm}
-    if world > 1:
-        sweep = {n: timed_med(stepper(n), 3, dev, world) for n in NANO_SWEEP if n <= n_tiles}
-        ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
-        horizons = []
-        for _ in range(8):
-            n = ctl.n
-            t = timed(stepper(n), 3, dev, world)
-            nxt, why = ctl.observe(t)
-            horizons.append({"n": n, "ms": round(t, 4), "decision": why, "next_n": nxt})
-        best_n = min(sweep, key=sweep.get)
-        if ctl.best_ms < sweep[best_n] and ctl.best_n in sweep:
-            best_n = ctl.best_n
-        res["n_sweep_ms"] = {str(k): round(v, 4) for k, v in sweep.items()}
-        res["aimd"] = horizons
-        res["aimd_best_n"] = ctl.best_n
-    else:
-        best_n = 1
-    launches0 = _lib.launch_count()
-    ms = timed_med(stepper(best_n), args.steps, dev, world)
-    res["gpu_launches_per_step"] = round((_lib.launch_count() - launches0) / (3 * args.steps), 2)
-    res["n"] = best_n
-    res["ms_per_step"] = round(ms, 4)
-    if world > 1:
-        t_compute = timed_med(stepper(best_n, comm_on=False), 3, dev, world)
-        t_serial = timed_med(stepper(best_n, pipelined=False), 3, dev, world) if comm == "nccl" else None
-        y_buf, ctx = layer.forward(x_p, plan, best_n)
-        t_comm = timed_med(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev, world)
-        res["overlap"] = {"pipelined_ms": round(ms, 4), "compute_only_ms": round(t_compute, 4),
-                          "comm_only_ms": round(t_comm, 4),
-                          "serial_ms": round(t_serial, 4) if t_serial is not None else None,
-                          "comm_hidden_frac": round(1.0 - max(0.0, ms - t_compute) / t_comm, 4) if t_comm > 0 else None,
-                          "comm_only_path": "multicast" if comm == "mc" else "nccl"}
-    res["timeline_ms"] = one_timeline(layer, stepper(best_n), dev)
-    _lib.clear_device_error()
-    res["parity"] = ksharded_parity(layer, w, x_p, plan, best_n, world, dev)
-    torch.cuda.synchronize(dev)
-    res["device_error"] = _lib.device_error()
+    try:
+        if world > 1:
+            sweep = {n: timed_med(graphed(n), 3, dev, world) for n in NANO_SWEEP if n <= n_tiles}
+            ctl = AIMDController(start_n=1, alpha=4, beta=0.5, tau_ms=0.05, max_n=min(32, n_tiles))
+            horizons = []
+            for _ in range(8):
+                n = ctl.n
+                t = timed(graphed(n), 3, dev, world)
+                nxt, why = ctl.observe(t)
+                horizons.append({"n": n, "ms": round(t, 4), "decision": why, "next_n": nxt})
+            best_n = min(sweep, key=sweep.get)
+            if ctl.best_ms < sweep[best_n] and ctl.best_n in sweep:
+                best_n = ctl.best_n
+            res["n_sweep_ms"] = {str(k): round(v, 4) for k, v in sweep.items()}
+            res["aimd"] = horizons
+            res["aimd_best_n"] = ctl.best_n
+        else:
+            best_n = 1
+        ms = timed_med(graphed(best_n), args.steps, dev, world)
+        res["n"] = best_n
+        res["ms_per_step"] = round(ms, 4)
+        launches0 = _lib.launch_count()
+        eager_ms, host_ms = host_and_device(stepper(best_n), args.steps, dev, world)
+        res["gpu_launches_per_step"] = round((_lib.launch_count() - launches0) / args.steps, 2)
+        res["eager"] = {"ms_per_step": round(eager_ms, 4), "host_enqueue_ms_per_step": round(host_ms, 4)}
+        if world > 1:
+            t_compute = timed_med(graphed(best_n, comm_on=False), 3, dev, world)
+            t_serial = timed_med(stepper(best_n, pipelined=False), 3, dev, world) if comm == "nccl" else None
+            y_buf, ctx = layer.forward(x_p, plan, best_n)
+            t_comm = timed_med(lambda: comm_only(layer, y_buf, ctx["z"], n_tiles, best_n), 3, dev, world)
+            res["overlap"] = {"pipelined_ms": round(ms, 4), "compute_only_ms": round(t_compute, 4),
+                              "comm_only_ms": round(t_comm, 4),
+                              "serial_ms_eager": round(t_serial, 4) if t_serial is not None else None,
+                              "comm_hidden_frac": (round(1.0 - max(0.0, ms - t_compute) / t_comm, 4)
+                                                   if t_comm > 0 else None),
+                              "comm_only_path": "multicast" if comm == "mc" else "nccl"}
+        res["timeline_ms"] = one_timeline(layer, stepper(best_n), dev)
+        _lib.clear_device_error()
+        res["parity"] = ksharded_parity(layer, w, x_p, plan, best_n, world, dev, step=graphed(best_n))
+        torch.cuda.synchronize(dev)
+        res["device_error"] = _lib.device_error()
+    finally:
+        torch.cuda.synchronize(dev)
+        graphs.clear()  # before the layer's buffers are released
     return res
 
 
 def e2e_ksharded(layer, w, x_p, plan, n, args, dev, world):
-    """End to end through the public API (ShardedLayer.step) with host
-    buffers: every step copies this rank's X shard from pinned host memory (on
-    a copy stream, double-buffered: the copy of step i + 1 overlaps step i, as
-    a data loader's prefetch does) and reads a probe of the updated adapter
-    weights back to the host (waited for one step later, as a training loop
-    logs its loss; the last read inside the timed region).  Device time over
-    the loop, barrier and max over ranks."""
+    """End to end through the public API (a GraphedShardedStep per input
+    buffer) with host buffers: every step copies this rank's X shard from
+    pinned host memory (on a copy stream, double-buffered: the copy of step
+    i + 1 overlaps step i, as a data loader's prefetch does) and reads a probe
+    of the updated adapter weights back to the host (waited for one step
+    later, as a training loop logs its loss; the last read inside the timed
+    region).  Device time over the loop, barrier and max over ranks."""
+    from tlora_b200.overlap import GraphedShardedStep
+
     x_host = x_p.detach().cpu().pin_memory()
-    bufs = [torch.empty_like(x_p) for _ in range(2)]
+    bufs = [x_p.clone() for _ in range(2)]
+    steps = [GraphedShardedStep(layer, b, plan, w.dy, n, w.spec.lr) for b in bufs]
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     copy_stream = torch.cuda.Stream(dev)
@@ -595,7 +658,7 @@ def e2e_ksharded(layer, w, x_p, plan, n, args, dev, world):
         state["i"] += 1
         compute.wait_event(copied[i % 2])
         issue_copy(i + 1)
-        layer.step(bufs[i % 2], plan, w.dy, n, w.spec.lr)
+        steps[i % 2]()
         consumed[i % 2].record(compute)
         probes[i % 2].copy_(layer.A_pack[0, :64], non_blocking=True)
         read[i % 2].record(compute)
@@ -611,8 +674,9 @@ def e2e_ksharded(layer, w, x_p, plan, n, args, dev, world):
     ms = timed(step, n_e2e, dev, world)
     torch.cuda.synchronize(dev)
     out = {"ms_per_step": round(ms, 4), "h2d_bytes_per_step": int(x_p.numel() * x_p.element_size()) * world,
-           "d2h_bytes_per_step": int(probes[0].numel() * probes[0].element_size()) * world}
-    del bufs
+           "d2h_bytes_per_step": int(probes[0].numel() * probes[0].element_size()) * world,
+           "path": "GraphedShardedStep replays, X shard copied from pinned host memory each step"}
+    del steps, bufs
     return out
 
 
@@ -638,7 +702,7 @@ def zsave_bytes(layer, x_p, plan):
 
 def run_ours(args, peaks_d, peaks_kind):
     from tlora_b200 import _lib, ops, workloads
-    from tlora_b200.overlap import NativeCompute, ShardedLayer
+    from tlora_b200.overlap import GraphedShardedStep, NativeCompute, ShardedLayer
 
     world, rank, local = _world()
     dev = torch.device("cuda", local)
@@ -681,17 +745,19 @@ def run_ours(args, peaks_d, peaks_kind):
         if clocks:
             clocks.start()
             time.sleep(0.3)
-        launches0 = _lib.launch_count()
-        ms = timed_med(lambda: layer.step(x_p, plan, w.dy, n, sp.lr), args.steps, dev, world)
-        launches = (_lib.launch_count() - launches0) // 3  # launches of one timed region of K steps
+        graph = GraphedShardedStep(layer, x_p, plan, w.dy, n, sp.lr)
+        ms = timed_med(graph, args.steps, dev, world)
+        launches = graph.kernels * args.steps  # this library's kernels in one timed region of K replays
         ck = clocks.stop() if clocks else None
-        # per-kernel device times of this rank (second pass, library events on)
-        kinds = kernel_times(lambda: layer.step(x_p, plan, w.dy, n, sp.lr), max(3, args.steps // 2))
+        del graph
+        # per-kernel device times of this rank (an eager pass, library events on)
+        ksteps = max(3, args.steps // 2)
+        kinds = kernel_times(lambda: layer.step(x_p, plan, w.dy, n, sp.lr), ksteps)
         kinds = {k: (v[0], v[1]) for k, v in kinds.items()}
         e2e = e2e_ksharded(layer, w, x_p, plan, n, args, dev, world)
         layer.close()
         zb = zsave_bytes(layer, x_p, plan)
-        roofs = rooflines(sp, kinds, zb, peaks_d, peaks_kind, world)
+        roofs = rooflines(sp, kinds, zb, peaks_d, peaks_kind, world, steps=ksteps)
         cub = None
         if not args.no_cublas:
             cub = cublas_backbone(x_p, layer.W, w.dy, dev)
@@ -730,7 +796,8 @@ def run_ours(args, peaks_d, peaks_kind):
             "step_frac_of_peak": round(sp.flops() / world / (ms / 1000.0) / 1e12 / float(peaks_d["bf16_tflops"]), 4),
             "roofline": roof,
             "rooflines": roofs,
-            "kernels_ms_per_step": {k: round(v[0] / max(3, args.steps // 2), 4) for k, v in kinds.items()},
+            "kernels_ms_per_step": {k: round(v[0] / ksteps, 4) for k, v in kinds.items()},
+            "step_replay": "CUDA graph of the whole step (GraphedShardedStep); the eager step is in ksharded.<path>.eager",
             "cublas_backbone": cub,
             "mainloop_vs_cublas": vs_cublas(roofs, cub),
             "e2e": {"value": round(sp.rows / (e2e["ms_per_step"] / 1000.0), 1), "unit": UNIT, **e2e},
@@ -785,13 +852,14 @@ def module_workloads(args, dev, peaks_d, peaks_kind):
                 for _ in range(max(3, args.warmup)):
                     fn()
                 ms = timed(fn, args.steps, dev, 1)
-                kinds = kernel_times(fn, max(3, args.steps // 2))
+                ksteps = max(3, args.steps // 2)
+                kinds = kernel_times(fn, ksteps)
             A_pack, B_pack, table = m.packed()
             plan = ops.route(ids_host, table, dev)
             sc = np.array([float(a.scaling) for a in m.adapters.values()], dtype=np.float32)
             zb = ops._CallArgs(sp.rows, sp.d_in, sp.d_out, ops.mlora_dtype(sp.dtype), "auto", plan, table,
                                sc).sizes()[0]
-            roofs = rooflines(sp, kinds, zb, peaks_d, peaks_kind)
+            roofs = rooflines(sp, kinds, zb, peaks_d, peaks_kind, steps=ksteps)
             cub = None if args.no_cublas else cublas_backbone(w.x.detach(), m.base.weight.detach(), w.dy, dev)
             out[name] = {"config": module_config(sp), "value": round(sp.rows / (ms / 1000.0), 1), "unit": UNIT,
                          "ms_per_step": round(ms, 4),

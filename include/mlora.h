@@ -242,17 +242,19 @@ int mlora_ar_wait(const mlora_peer_ar* ar, void* stream);
  * ranks have said so, and sums this rank's 1/world share of the rows in place
  * with multimem.ld_reduce (fp32 accumulation in the switch, one rounding) and
  * multimem.st (the sum lands in every rank's Y).  `slot` identifies the
- * nano-batch within a step (< MLORA_MC_SLOTS) and `use` counts this slot's
- * uses, 1, 2, ... (the same on every rank).  mlora_mc_wait(n_slots, uses)
- * waits (bounded) until every rank has written its sums of slots
- * [0, n_slots) into this rank's Y; the caller's stream must wait for it
- * before Y is read or the next forward rewrites it.  Every wait of a launch
+ * nano-batch within a step (< MLORA_MC_SLOTS); the flag words count each
+ * slot's uses on the device, so every rank must make the same sequence of
+ * calls, and a captured CUDA graph replays with the right targets.
+ * mlora_mc_wait(n_slots) waits (bounded) until every rank has written its
+ * sums of slots [0, n_slots) of the latest uses into this rank's Y; the
+ * caller's stream must wait for it before Y is read or the next forward
+ * rewrites it.  Every wait of a launch
  * gives up at one deadline (timeout_ns, 0 = 2 s), sets the timeout bit of
  * err_word (or of the library-wide word) and lets the launch finish.
  * Requires 16-bit dtypes and d_out % 8 == 0.  No counterpart beyond the
  * reference's all-reduce. */
 #define MLORA_MC_SLOTS 64
-#define MLORA_MC_FLAG_WORDS (3 * MLORA_MC_SLOTS)
+#define MLORA_MC_FLAG_WORDS (4 * MLORA_MC_SLOTS)
 typedef struct mlora_mc_ar {
   int32_t rank, world;
   int64_t rows;          /* rows of Y */
@@ -264,12 +266,16 @@ typedef struct mlora_mc_ar {
   int64_t timeout_ns;
   int32_t* err_word;     /* optional DEVICE int32 for this rank's flags; NULL = library-wide word */
 } mlora_mc_ar;
-int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int64_t row_end, int32_t slot, uint32_t use,
-                       void* stream);
-int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, const uint32_t* uses, void* stream);
+int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int64_t row_end, int32_t slot, void* stream);
+int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, void* stream);
 
 /* Peer memory for the buffers above: one cudaMalloc'd block per rank, shared
- * with the other processes by CUDA IPC (64-byte handles). */
+ * with the other processes by CUDA IPC (64-byte handles).  mlora_peer_copy
+ * copies `bytes` (a multiple of 16, 16-byte aligned pointers) with plain
+ * 16-byte loads and stores from every SM; either side may be a peer mapping,
+ * which measures the link bandwidth between two ranks (no counterpart in the
+ * reference). */
+int mlora_peer_copy(void* dst, const void* src, size_t bytes, void* stream);
 int mlora_peer_alloc(size_t bytes, void** ptr);
 int mlora_peer_free(void* ptr);
 int mlora_ipc_handle(void* ptr, void* handle64);

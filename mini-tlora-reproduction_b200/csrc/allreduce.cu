@@ -11,6 +11,7 @@
 // all-reduce of the output rows (phase6_two_gpu_overlap.py:247-280) as one
 // reduce-scatter issued from the GEMM epilogue plus an owner-side gather; no
 // TMA and no multicast are involved.
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -198,6 +199,21 @@ __global__ void k_ar_wait(const __grid_constant__ ArWait w) {
   if (!ar_wait_count(w.done, w.target, deadline) && threadIdx.x == 0) flag_error(w.err, kErrTimeout);
 }
 
+// dst[i] = src[i] for n 16-byte units, grid-stride, four loads in flight per
+// thread (plain loads and stores; either side may be a peer mapping)
+__global__ void __launch_bounds__(512) k_copy16(uint4* __restrict__ dst, const uint4* __restrict__ src, int64_t n) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n; i += 4 * stride) {
+    const uint4 a = src[i], b = src[i + stride], c = src[i + 2 * stride], d = src[i + 3 * stride];
+    dst[i] = a;
+    dst[i + stride] = b;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < n; i += stride) dst[i] = src[i];
+}
+
 int lt_stride_of(int n_tiles, int world) { return (n_tiles + world - 1) / world; }
 
 // The finish and wait kernels use no shared memory, yet ask for the largest
@@ -326,6 +342,21 @@ extern "C" int mlora_ar_wait(const mlora_peer_ar* ar, void* stream) {
   k_ar_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+extern "C" int mlora_peer_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!dst || !src || bytes % 16 != 0) return MLORA_ERR_INVALID_ARG;
+  if (!aligned(dst, 16) || !aligned(src, 16)) return MLORA_ERR_UNSUPPORTED;
+  if (bytes == 0) return MLORA_OK;
+  int dev = 0, sms = 0;
+  MLORA_CUDA_TRY(cudaGetDevice(&dev));
+  MLORA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t n = int64_t(bytes / 16);
+  const int grid = int(std::min<int64_t>(2 * sms, (n + 511) / 512));
+  k_copy16<<<grid, 512, 0, (cudaStream_t)stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), n);
+  MLORA_CUDA_TRY(cudaGetLastError());
+  count_launch();
+  return MLORA_OK;
 }
 
 extern "C" int mlora_peer_alloc(size_t bytes, void** ptr) {

@@ -19,16 +19,21 @@
 // same switch operations.
 //
 // Ordering across ranks, per nano-batch slot s (a nano-batch index of the
-// step; `use` counts the uses of a slot, the same on every rank):
+// step), with use[s] the number of times this rank has used slot s (a device
+// counter of its own, the same on every rank since every rank runs the same
+// sequence of calls):
 //   * k_mc_signal (after the rank's mainloop of the nano-batch, stream order):
-//     one release-add of 1 to ready[s] on every rank (multimem.red);
+//     use[s] += 1, then one release-add of 1 to ready[s] on every rank
+//     (multimem.red);
 //   * k_mc_reduce: every CTA waits (bounded) until its own ready[s] reaches
-//     world * use, i.e. every rank's partial rows are in place, sums its share
-//     and, once all its CTAs are done (a self-resetting CTA counter), adds 1
-//     to done[s] on every rank;
-//   * k_mc_wait: waits (bounded) until done[s] reaches world * use for every
+//     world * use[s], i.e. every rank's partial rows are in place, sums its
+//     share and, once all its CTAs are done (a self-resetting CTA counter),
+//     adds 1 to done[s] on every rank;
+//   * k_mc_wait: waits (bounded) until done[s] reaches world * use[s] for every
 //     slot of the step, i.e. every rank has written its sums into this rank's
 //     Y; the caller's stream waits for it before Y is read or rewritten.
+// The targets live on the device, so a step captured in a CUDA graph replays
+// with the right targets.
 // A rank cannot start the next step's mainloop (which rewrites its partial
 // rows) before its k_mc_wait of this step, and the counters only grow, so no
 // reset or barrier is needed between steps.  Every wait gives up at one
@@ -46,16 +51,17 @@ namespace {
 constexpr int kMcThreads = 512;
 constexpr int kMcUnroll = 4;  // 16-byte units in flight per thread
 constexpr unsigned long long kMcDefaultTimeoutNs = 2000000000ull;
-// flag words: ready[s] at s, done[s] at MLORA_MC_SLOTS + s, CTA counter of the
-// rank's own reduce launch of slot s at 2 MLORA_MC_SLOTS + s (local only)
-constexpr int kReady = 0, kDone = MLORA_MC_SLOTS, kCtas = 2 * MLORA_MC_SLOTS;
+// flag words: ready[s] at s, done[s] at MLORA_MC_SLOTS + s, and, used through
+// this rank's own copy only, the CTA counter of the rank's reduce launch of
+// slot s at 2 MLORA_MC_SLOTS + s and use[s] at 3 MLORA_MC_SLOTS + s
+constexpr int kReady = 0, kDone = MLORA_MC_SLOTS, kCtas = 2 * MLORA_MC_SLOTS, kUses = 3 * MLORA_MC_SLOTS;
 
 struct McReduce {
   uint8_t* y_mc;          // multicast address of Y
   uint32_t* flags_mc;     // multicast address of the flag words
   uint32_t* flags;        // this rank's flag words
   int64_t u0, u1;         // 16-byte units of Y this rank sums: [u0, u1)
-  unsigned target;        // world * use
+  unsigned world;
   unsigned long long timeout_ns;
   int slot, f16;
   int* err;
@@ -63,7 +69,7 @@ struct McReduce {
 
 struct McWait {
   const uint32_t* flags;
-  unsigned target[MLORA_MC_SLOTS];
+  unsigned world;
   int n_slots;
   unsigned long long timeout_ns;
   int* err;
@@ -99,8 +105,12 @@ __device__ bool mc_wait_word(const uint32_t* word, unsigned target, unsigned lon
   }
 }
 
-__global__ void k_mc_signal(uint32_t* word_mc) {
-  if (threadIdx.x == 0) mc_signal_all(word_mc);
+// this rank's partial rows of slot s are in place: count the use, tell every rank
+__global__ void k_mc_signal(uint32_t* flags_mc, uint32_t* flags, int slot) {
+  if (threadIdx.x == 0) {
+    flags[kUses + slot] += 1;
+    mc_signal_all(flags_mc + kReady + slot);
+  }
 }
 
 __device__ __forceinline__ uint4 mc_ld_reduce(const uint8_t* p, int f16) {
@@ -129,7 +139,8 @@ __global__ void __launch_bounds__(kMcThreads) k_mc_reduce(const __grid_constant_
   __shared__ int ok;
   const unsigned long long deadline = mc_now() + a.timeout_ns;
   if (threadIdx.x == 0) {
-    ok = mc_wait_word(a.flags + kReady + a.slot, a.target, deadline) ? 1 : 0;
+    const unsigned target = a.world * a.flags[kUses + a.slot];  // counted by k_mc_signal before this launch
+    ok = mc_wait_word(a.flags + kReady + a.slot, target, deadline) ? 1 : 0;
     if (!ok) flag_error(a.err, kErrTimeout);
   }
   __syncthreads();
@@ -159,7 +170,7 @@ __global__ void k_mc_wait(const __grid_constant__ McWait w) {
   if (threadIdx.x != 0) return;
   const unsigned long long deadline = mc_now() + w.timeout_ns;
   for (int s = 0; s < w.n_slots; ++s) {
-    if (!mc_wait_word(w.flags + kDone + s, w.target[s], deadline)) {
+    if (!mc_wait_word(w.flags + kDone + s, w.world * w.flags[kUses + s], deadline)) {
       flag_error(w.err, kErrTimeout);
       return;
     }
@@ -186,11 +197,11 @@ unsigned long long mc_timeout(const mlora_mc_ar* ar) {
 using namespace mlora;
 
 extern "C" int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int64_t row_end, int32_t slot,
-                                  uint32_t use, void* stream) {
+                                  void* stream) {
   int st = check_mc(ar);
   if (st != MLORA_OK) return st;
   if (row_begin < 0 || row_end < row_begin || row_end > ar->rows) return MLORA_ERR_INVALID_ARG;
-  if (slot < 0 || slot >= MLORA_MC_SLOTS || use < 1) return MLORA_ERR_INVALID_ARG;
+  if (slot < 0 || slot >= MLORA_MC_SLOTS) return MLORA_ERR_INVALID_ARG;
   McReduce a = {};
   a.y_mc = static_cast<uint8_t*>(ar->y_mc);
   a.flags_mc = ar->flags_mc;
@@ -199,7 +210,7 @@ extern "C" int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int6
   const int64_t first = row_begin * int64_t(ar->d_out) / 8;
   a.u0 = first + units * ar->rank / ar->world;
   a.u1 = first + units * (ar->rank + 1) / ar->world;
-  a.target = unsigned(ar->world) * use;
+  a.world = unsigned(ar->world);
   a.timeout_ns = mc_timeout(ar);
   a.slot = slot;
   a.f16 = ar->dtype == MLORA_F16 ? 1 : 0;
@@ -215,7 +226,7 @@ extern "C" int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int6
   MLORA_CUDA_TRY(max_carveout_once(reinterpret_cast<const void*>(&k_mc_reduce)));
   // this rank's partial rows of the slot are in place (the stream orders the
   // mainloop that wrote them before this launch)
-  k_mc_signal<<<1, 32, 0, s>>>(ar->flags_mc + kReady + slot);
+  k_mc_signal<<<1, 32, 0, s>>>(ar->flags_mc, ar->flags, slot);
   MLORA_CUDA_TRY(cudaGetLastError());
   k_mc_reduce<<<grid, kMcThreads, 0, s>>>(a);
   MLORA_CUDA_TRY(cudaGetLastError());
@@ -223,15 +234,15 @@ extern "C" int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int6
   return MLORA_OK;
 }
 
-extern "C" int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, const uint32_t* uses, void* stream) {
+extern "C" int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, void* stream) {
   int st = check_mc(ar);
   if (st != MLORA_OK) return st;
-  if (n_slots < 0 || n_slots > MLORA_MC_SLOTS || (n_slots > 0 && !uses)) return MLORA_ERR_INVALID_ARG;
+  if (n_slots < 0 || n_slots > MLORA_MC_SLOTS) return MLORA_ERR_INVALID_ARG;
   if (n_slots == 0) return MLORA_OK;
   McWait w = {};
   w.flags = ar->flags;
+  w.world = unsigned(ar->world);
   w.n_slots = n_slots;
-  for (int s = 0; s < n_slots; ++s) w.target[s] = unsigned(ar->world) * uses[s];
   w.timeout_ns = mc_timeout(ar);
   w.err = ar->err_word;
   k_mc_wait<<<1, 32, 0, (cudaStream_t)stream>>>(w);

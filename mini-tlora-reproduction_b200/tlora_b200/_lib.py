@@ -99,7 +99,7 @@ class PeerAr(ctypes.Structure):
 
 
 MC_SLOTS = 64
-MC_FLAG_WORDS = 3 * MC_SLOTS
+MC_FLAG_WORDS = 4 * MC_SLOTS
 
 
 class McAr(ctypes.Structure):
@@ -150,9 +150,9 @@ SIGNATURES = {
     "mlora_ar_finish": (ctypes.c_int, [ctypes.POINTER(PeerAr), ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _VP]),
     "mlora_ar_wait": (ctypes.c_int, [ctypes.POINTER(PeerAr), _VP]),
-    "mlora_mc_allreduce": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
-                                          ctypes.c_uint32, _VP]),
-    "mlora_mc_wait": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32), _VP]),
+    "mlora_mc_allreduce": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _VP]),
+    "mlora_mc_wait": (ctypes.c_int, [ctypes.POINTER(McAr), ctypes.c_int32, _VP]),
+    "mlora_peer_copy": (ctypes.c_int, [_VP, _VP, ctypes.c_size_t, _VP]),
     "mlora_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "mlora_peer_free": (ctypes.c_int, [_VP]),
     "mlora_ipc_handle": (ctypes.c_int, [_VP, _VP]),

@@ -498,9 +498,22 @@ class MultiLoRAFunction(torch.autograd.Function):
         return (dx, None, None, None, *grads)
 
 
-def sgd_step_(params_and_grads, lr: float) -> int:
-    """P <- P - lr * G for the listed (param, grad) pairs in one launch per 64
-    tensors (mlora_sgd).  Params are 2-D views with unit column stride."""
+class SgdItems:
+    """The item array of ``mlora_sgd`` for a fixed list of (param, grad)
+    pairs, built once; ``step(lr)`` is one launch with no per-call host
+    work beyond the call.  The tensors must stay alive and in place."""
+
+    def __init__(self, params_and_grads):
+        self.items, self.dtype, self.device, self.keep = _sgd_items(params_and_grads)
+
+    def step(self, lr: float) -> int:
+        if self.items is None:
+            return 0
+        _lib.call("mlora_sgd", self.items, len(self.items), float(lr), self.dtype, _stream(self.device))
+        return len(self.items)
+
+
+def _sgd_items(params_and_grads):
     items = []
     dtype = None
     device = None
@@ -517,10 +530,14 @@ def sgd_step_(params_and_grads, lr: float) -> int:
             dtype, device = dt, p.device
         elif dt != dtype or p.device != device:
             raise ValueError("all tensors of one sgd_step_ call share a dtype and a device")
-        keep.append(g)
+        keep.append((p, g))
         items.append(_lib.SgdItem(p.data_ptr(), g.data_ptr(), p.shape[0], p.shape[1], p.stride(0), g.stride(0)))
     if not items:
-        return 0
-    arr = (_lib.SgdItem * len(items))(*items)
-    _lib.call("mlora_sgd", arr, len(items), float(lr), dtype, _stream(device))
-    return len(items)
+        return None, dtype, device, keep
+    return (_lib.SgdItem * len(items))(*items), dtype, device, keep
+
+
+def sgd_step_(params_and_grads, lr: float) -> int:
+    """P <- P - lr * G for the listed (param, grad) pairs in one launch per 64
+    tensors (mlora_sgd).  Params are 2-D views with unit column stride."""
+    return SgdItems(params_and_grads).step(lr)

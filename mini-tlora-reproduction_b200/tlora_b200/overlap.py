@@ -191,14 +191,21 @@ class NativeCompute:
         b["bw"].run_all()
 
     def sgd(self, layer, plan, dA_p, dB, lr):
-        pairs = []
-        for i in range(layer.table.n):
-            if not plan.active[i]:
-                continue
-            o, r = int(layer.table.pack_off[i]), int(layer.table.rank[i])
-            pairs.append((layer.A_pack[o:o + r], dA_p[o:o + r]))
-            pairs.append((layer.B_pack[:, o:o + r], dB[:, o:o + r]))
-        return ops.sgd_step_(pairs, lr)
+        """Isolated SGD of the plan's active adapters, one launch; the item
+        list (pointers into the layer's weights and the reused gradient
+        buffers) is built once per plan and buffers."""
+        key = (id(plan), layer.A_pack.data_ptr(), layer.B_pack.data_ptr(), dA_p.data_ptr(), dB.data_ptr())
+        c = getattr(self, "_sgd", None)
+        if c is None or c[0] != key:
+            pairs = []
+            for i in range(layer.table.n):
+                if not plan.active[i]:
+                    continue
+                o, r = int(layer.table.pack_off[i]), int(layer.table.rank[i])
+                pairs.append((layer.A_pack[o:o + r], dA_p[o:o + r]))
+                pairs.append((layer.B_pack[:, o:o + r], dB[:, o:o + r]))
+            c = self._sgd = (key, ops.SgdItems(pairs), plan)
+        return c[1].step(lr)
 
 
 class ShardedLayer:
@@ -585,3 +592,48 @@ def comm_only(layer: ShardedLayer, y: torch.Tensor, z: Optional[torch.Tensor], n
             works.append(dist.all_reduce(seg, op=dist.ReduceOp.SUM, group=layer.group, async_op=True))
     for w in works:
         w.wait()
+
+
+class GraphedShardedStep:
+    """CUDA-graph replay of ``ShardedLayer.step`` for fixed routing, input
+    buffers and nano-batch count: every kernel, every all-reduce (NCCL's
+    collectives, or the peer / multicast kernels on their side stream) and
+    the stream forks and joins of one step are captured once and replayed with
+    one launch, so a step costs no host work.  Every rank of the layer's group
+    builds its graph at the same point (capture runs one eager step on each
+    rank first).  ``x_p`` and ``dy`` are the graph's input buffers: copy new
+    inputs into them before a replay; Y, dX_p and the gradients live in the
+    layer's buffers and are overwritten by the next replay."""
+
+    def __init__(self, layer: "ShardedLayer", x_p, plan, dy, n_nano: int, lr: float, warmup: int = 2,
+                 pipelined: bool = True, comm: bool = True):
+        dev = x_p.device
+        self.layer, self.x, self.plan, self.dy, self.n, self.lr = layer, x_p, plan, dy, int(n_nano), float(lr)
+        kw = {"pipelined": pipelined, "comm": comm}
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up off the default stream, as capture requires
+            for _ in range(max(1, warmup)):
+                layer.step(x_p, plan, dy, self.n, self.lr, **kw)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        # the captured step must not wait on events recorded outside the capture
+        layer._last_done = None
+        layer._pending = None
+        if layer.world > 1:
+            dist.barrier(group=layer.group)
+        self.graph = torch.cuda.CUDAGraph()
+        launches0 = _lib.launch_count()
+        # thread-local capture: other threads of the process (NCCL's watchdog)
+        # keep making CUDA calls while this one captures
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+            self.y, self.dx = layer.step(x_p, plan, dy, self.n, self.lr, **kw)
+        self.kernels = _lib.launch_count() - launches0  # this library's kernels in one replay
+        layer._last_done = None
+        layer._pending = None
+        self.grads = layer.last_grads
+
+    def __call__(self):
+        """Replay one step on the current stream; returns (Y, dX_p)."""
+        self.graph.replay()
+        return self.y, self.dx

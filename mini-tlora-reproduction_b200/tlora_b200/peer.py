@@ -224,7 +224,6 @@ class MulticastAllReduce:
         self.ar.flags_mc = mc + off + y_bytes
         self.ar.flags = self.buf.data_ptr() + y_bytes
         self.ar.timeout_ns = int(timeout_s * 1e9)
-        self.uses = [0] * _lib.MC_SLOTS
         self._err_word = None
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every rank's flags are zero before any rank signals
@@ -248,16 +247,14 @@ class MulticastAllReduce:
     def reduce(self, r0: int, r1: int, slot: int, stream=None) -> None:
         """Sum rows [r0, r1) of ``y`` across the ranks, in place, as nano-batch
         ``slot`` of the step (after this rank's partial rows are written, in
-        the order of ``stream``)."""
-        self.uses[slot] += 1
-        _lib.call("mlora_mc_allreduce", ctypes.byref(self.ar), int(r0), int(r1), int(slot), self.uses[slot],
+        the order of ``stream``).  Every rank makes the same sequence of calls."""
+        _lib.call("mlora_mc_allreduce", ctypes.byref(self.ar), int(r0), int(r1), int(slot),
                   _stream_handle(stream, self.device))
 
     def wait(self, n_slots: int, stream=None) -> None:
         """``stream`` waits until every rank's sums of slots [0, n_slots) are in
         this rank's ``y``."""
-        uses = (ctypes.c_uint32 * max(1, n_slots))(*self.uses[:n_slots])
-        _lib.call("mlora_mc_wait", ctypes.byref(self.ar), int(n_slots), uses, _stream_handle(stream, self.device))
+        _lib.call("mlora_mc_wait", ctypes.byref(self.ar), int(n_slots), _stream_handle(stream, self.device))
 
     def close(self) -> None:
         """Release the buffer (collective: after every rank's device work)."""

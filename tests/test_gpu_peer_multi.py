@@ -9,7 +9,8 @@ the unsharded layer within 2e-2 (Y, dX and dA gathered from the ranks'
 shards, dB, the updated weights) with the SGD update elementwise, as the
 reference checks its GPU training path (phase5d_triton_training.py:420-589);
 the peer and multicast forwards must equal NCCL's up to the rounding of the
-bf16 sum.  Needs >= 2 GPUs; NVLink multicast objects are used only by the
+bf16 sum.  Each path is also checked replayed from a CUDA graph of the whole
+step (GraphedShardedStep), replayed twice.  Needs >= 2 GPUs; NVLink multicast objects are used only by the
 multicast case, whose ranks all finish their device work before any exits."""
 
 import os
@@ -47,19 +48,20 @@ def _worker(rank, world, port, q):
 
         out = {}
         for comm in COMMS:
-            try:
-                res = run_rank_comm(rank, world, comm, dev)
-            except RuntimeError as e:
-                if comm == "mc" and "multicast" in str(e):
-                    res = {"unsupported": str(e)}
-                else:
-                    raise
-            out[comm] = res
+            for graphed in (False, True):
+                try:
+                    res = run_rank_comm(rank, world, comm, dev, graphed)
+                except RuntimeError as e:
+                    if comm == "mc" and "multicast" in str(e):
+                        res = {"unsupported": str(e)}
+                    else:
+                        raise
+                out[(comm, graphed)] = res
         # forwards of the three paths on the same inputs
         w = workloads.build(_spec(), device=dev)
         fw = {}
         for comm in COMMS:
-            if "unsupported" in out.get(comm, {}):
+            if "unsupported" in out.get((comm, False), {}):
                 continue
             layer = ShardedLayer(w.model, rank, world, comm=comm)
             plan = ops.route(w.ids.cpu(), layer.table, dev)
@@ -75,25 +77,41 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def run_rank_comm(rank, world, comm, dev):
+def run_rank_comm(rank, world, comm, dev, graphed=False):
     """run_rank of test_gpu_ksharded with the given all-reduce path (one
-    step, 3 nano-batches) on the default NCCL group."""
+    step, 3 nano-batches) on the default NCCL group; with ``graphed`` the
+    step is replayed from a CUDA graph (GraphedShardedStep) after the
+    weights are reset to the model's."""
     from test_gpu_ksharded import _spec
     import numpy as np  # noqa: F811
     from tlora_b200 import _lib, ops, workloads
-    from tlora_b200.overlap import ShardedLayer
+    from tlora_b200.overlap import GraphedShardedStep, ShardedLayer
 
     w = workloads.build(_spec(), device=dev)
     bwd = dist.new_group(list(range(world)))
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     layer = ShardedLayer(w.model, rank, world, bwd_group=bwd, comm=comm, err_word=err)
+    g = None
     try:
         plan = ops.route(w.ids.cpu(), layer.table, dev)
         x_p = layer.shard_input(w.x)
-        y, dx_p = layer.step(x_p, plan, w.dy, 3, lr=w.spec.lr)
+        if graphed:
+            A0, B0 = layer.A_pack.clone(), layer.B_pack.clone()
+            g = GraphedShardedStep(layer, x_p, plan, w.dy, 3, w.spec.lr)
+            with torch.no_grad():
+                layer.A_pack.copy_(A0)
+                layer.B_pack.copy_(B0)
+            for _ in range(2):  # replay twice: the second replay must wait for the other rank's sums too
+                with torch.no_grad():
+                    layer.A_pack.copy_(A0)
+                    layer.B_pack.copy_(B0)
+                y, dx_p = g()
+            dA_p, dB = g.grads
+        else:
+            y, dx_p = layer.step(x_p, plan, w.dy, 3, lr=w.spec.lr)
+            dA_p, dB = layer.last_grads
         torch.cuda.synchronize(dev)
         layer.check()
-        dA_p, dB = layer.last_grads
 
         def f64(t):
             return t.detach().float().cpu().numpy().astype(np.float64)
@@ -102,6 +120,8 @@ def run_rank_comm(rank, world, comm, dev):
                 "B": f64(layer.B_pack), "cols": (layer.k0, layer.k1), "err": int(err.item()),
                 "lib_err": _lib.device_error()}
     finally:
+        torch.cuda.synchronize(dev)
+        del g  # the graph before the buffers it uses
         layer.close()
 
 
@@ -128,13 +148,14 @@ def test_ksharded_step_two_gpus_every_allreduce_path():
         assert p.exitcode == 0
     checked = []
     for comm in COMMS:
-        parts = [res[r][comm] for r in range(world)]
-        if any("unsupported" in p for p in parts):
-            assert comm == "mc"
-            continue
-        check_against_oracle(parts)
-        checked.append(comm)
-    assert "nccl" in checked and "peer" in checked
+        for graphed in (False, True):
+            parts = [res[r][(comm, graphed)] for r in range(world)]
+            if any("unsupported" in p for p in parts):
+                assert comm == "mc"
+                continue
+            check_against_oracle(parts)
+            checked.append((comm, graphed))
+    assert {("nccl", False), ("nccl", True), ("peer", False), ("peer", True)} <= set(checked)
     fw = res[0]["forwards"]
     ref = fw["nccl"]
     for comm, y in fw.items():
