@@ -98,6 +98,8 @@ typedef struct mlora_problem {
                         it.  NULL = the library-wide word of mlora_get_error.  Replaces the
                         exception a failing kernel raises through torch in the reference
                         (phase5c_fused_triton.py:524-540); no counterpart otherwise. */
+  float lr;          /* learning rate of the SGD step fused into the backward (MLORA_BWD_SGD_A /
+                        MLORA_BWD_SGD_B, MLORA_FUSED_SGD); unused otherwise */
 } mlora_problem;
 /* flags: the workspace already holds this problem's routing plan, written by
  * mlora_plan_upload with the same problem and routing; the call then issues
@@ -105,6 +107,9 @@ typedef struct mlora_problem {
  * sequence of calls can be captured into a CUDA graph and replayed.  The
  * caller keeps the workspace untouched between the upload and the calls. */
 #define MLORA_PLAN_RESIDENT 1
+/* flags: mlora_backward also applies the isolated SGD step to A_pack and
+ * B_pack (MLORA_BWD_SGD_A | MLORA_BWD_SGD_B below) with learning rate lr. */
+#define MLORA_FUSED_SGD 2
 
 typedef struct mlora_routing {
   int32_t n_seg;              /* number of contiguous row segments */
@@ -308,6 +313,9 @@ int mlora_forward_noalloc(const mlora_problem* prob, const mlora_routing* route,
                           const void* A_pack, const void* B_pack, void* Y, void* stream);
 
 /* Analytic backward.  Any of dX, dA_pack, dB_pack may be NULL to skip it.
+ * With MLORA_FUSED_SGD in prob->flags it also applies the isolated SGD step
+ * (MLORA_BWD_SGD_A | MLORA_BWD_SGD_B) to A_pack and B_pack, which it then
+ * writes despite their const qualifier.
  * W may be NULL: then dX holds only the LoRA term (delta-only forward).
  * dA_pack/dB_pack are written (not accumulated) for every adapter that owns at
  * least one row; entries of adapters with no rows are left untouched. */
@@ -323,6 +331,12 @@ int mlora_backward(const mlora_problem* prob, const mlora_routing* route,
 #define MLORA_BWD_DX 2  /* dX = dY W + dZ A over all rows (reads all of dzsave) */
 #define MLORA_BWD_DA 4  /* dA_pack = dZ^T X (reads all of dzsave) */
 #define MLORA_BWD_DB 8  /* dB_pack = dY^T Z for d_out rows [128 db_begin, 128 db_end) */
+#define MLORA_BWD_SGD_A 16  /* with DA: the reduction's epilogue also applies A <- A - lr dA (lr in the
+                               problem) to every element of A_pack whose gradient it writes, from the
+                               gradient as stored, so the result equals mlora_sgd over the same
+                               adapters (phase5d_triton_training.py:554-559) without a second pass.
+                               A_pack is updated in place. */
+#define MLORA_BWD_SGD_B 32  /* with DB: the same for B_pack and dB_pack */
 
 /* mlora_backward split into stages and ranges, with the dZ intermediate in a
  * caller-owned buffer dzsave (mlora_zsave_bytes bytes).  A K-sharded rank

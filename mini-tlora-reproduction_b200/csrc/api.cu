@@ -252,7 +252,11 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
   thread_local Plan p;
   int st = build_plan(prob, route, &p);
   if (st != MLORA_OK) return st;
-  if (stages & ~(MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB)) return MLORA_ERR_INVALID_ARG;
+  if (stages & ~(MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB | MLORA_BWD_SGD_A | MLORA_BWD_SGD_B))
+    return MLORA_ERR_INVALID_ARG;
+  // the fused SGD step updates the weights whose gradients the call writes
+  if ((stages & MLORA_BWD_SGD_A) && (!(stages & MLORA_BWD_DA) || !dA_pack || !A_pack)) return MLORA_ERR_INVALID_ARG;
+  if ((stages & MLORA_BWD_SGD_B) && (!(stages & MLORA_BWD_DB) || !dB_pack || !B_pack)) return MLORA_ERR_INVALID_ARG;
   const int nb_out = (prob->d_out + 127) / 128;
   if (tile_begin < 0 || tile_end < tile_begin || tile_end > p.n_tiles) return MLORA_ERR_INVALID_ARG;
   if (db_begin < 0 || db_end < db_begin || db_end > nb_out) return MLORA_ERR_INVALID_ARG;
@@ -286,6 +290,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
     a.max_ctas = prob->max_ctas;
     a.pair_dx = prob->impl != MLORA_IMPL_TC_1SM;
     a.bwd_stages = stages; a.t0 = tile_begin; a.t1 = tile_end; a.db0 = db_begin; a.db1 = db_end;
+    a.lr = prob->lr;
     return tc_backward(a, s);
   }
   SimtCall a;
@@ -298,6 +303,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
   a.zsave = (void*)zsave; a.dzt = dzsave; a.dX = dX; a.dA = dA_pack; a.dB = dB_pack;
   a.out_rows = route->out_rows;
   a.bwd_stages = stages; a.db0 = db_begin; a.db1 = db_end;
+  a.lr = prob->lr;
   a.c_begin = p.tile_chunk_begin[tile_begin];
   a.c_end = p.tile_chunk_begin[tile_end];
   return simt_backward(a, s);
@@ -317,10 +323,12 @@ extern "C" int mlora_backward(const mlora_problem* prob, const mlora_routing* ro
   }
   // dZ scratch lives in the workspace after the plan tables
   void* dzt = workspace ? (uint8_t*)workspace + align_up(plan_bytes, 1024) : nullptr;
+  int32_t stages = ((dX || dA_pack) ? MLORA_BWD_DZ : 0) | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB;
+  if (prob->flags & MLORA_FUSED_SGD)
+    stages |= (dA_pack ? MLORA_BWD_SGD_A : 0) | (dB_pack ? MLORA_BWD_SGD_B : 0);
   return mlora_backward_staged(prob, route, dY, X, W, A_pack, B_pack, zsave, dzt, dX, dA_pack, dB_pack,
-                               workspace, workspace_bytes,
-                               ((dX || dA_pack) ? MLORA_BWD_DZ : 0) | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB, 0,
-                               mlora_num_tiles(prob->rows), 0, (prob->d_out + 127) / 128, stream);
+                               workspace, workspace_bytes, stages, 0, mlora_num_tiles(prob->rows), 0,
+                               (prob->d_out + 127) / 128, stream);
 }
 
 extern "C" int mlora_sgd(const mlora_sgd_item* items, int32_t n_items, float lr, int32_t dtype,

@@ -126,6 +126,14 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
+// One element of the isolated SGD step fused into a gradient epilogue: the
+// update reads the gradient as it was stored (rounded to T), with the same
+// expression as the separate SGD pass, so both give the same bits.
+template <class T>
+__device__ __forceinline__ void sgd_apply(T* p, T g, float lr) {
+  *p = from_f<T>(to_f(*p) - lr * to_f(g));
+}
+
 }  // namespace mlora
 
 #define MLORA_CUDA_TRY(expr)                                   \

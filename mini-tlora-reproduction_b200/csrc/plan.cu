@@ -23,7 +23,7 @@ static int validate(const mlora_problem* prob, const mlora_routing* r) {
   if (prob->d_in < 1 || prob->d_out < 1) return MLORA_ERR_INVALID_ARG;
   if (prob->dtype != MLORA_F32 && prob->dtype != MLORA_BF16 && prob->dtype != MLORA_F16) return MLORA_ERR_UNSUPPORTED;
   if (prob->max_ctas < 0) return MLORA_ERR_INVALID_ARG;
-  if (prob->flags & ~MLORA_PLAN_RESIDENT) return MLORA_ERR_INVALID_ARG;
+  if (prob->flags & ~(MLORA_PLAN_RESIDENT | MLORA_FUSED_SGD)) return MLORA_ERR_INVALID_ARG;
   if (r->n_seg < 0 || r->n_adapters < 0) return MLORA_ERR_INVALID_ARG;
   if (r->r_pack < 0 || r->r_pack % kChunk) return MLORA_ERR_INVALID_ARG;
   if (r->n_seg > 0 && (!r->seg_start || !r->seg_adapter)) return MLORA_ERR_INVALID_ARG;

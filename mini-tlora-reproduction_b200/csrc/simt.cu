@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(NT) k_reduce(PlanDev plan, const T* __restrict
                                                 const T* __restrict__ dY, const T* __restrict__ zt,
                                                 const T* __restrict__ dzt, T* __restrict__ dA,
                                                 T* __restrict__ dB, int64_t M, int d_in, int d_out,
-                                                int R, int db0, int db1) {
+                                                int R, int db0, int db1, T* A_upd, T* B_upd, float lr) {
   __shared__ float As[BK][LD], Bs[BK][LD];
   const ReduceItem it = plan.reduce[blockIdx.x];
   const int jc = blockIdx.y;
@@ -208,10 +208,14 @@ __global__ void __launch_bounds__(NT) k_reduce(PlanDev plan, const T* __restrict
     for (int q = 0; q < 4; ++q) {
       const int jj = tx * 4 + q;
       if (jj >= rvalid) continue;
-      if (is_dB)
-        dB[int64_t(d) * R + pcol + jj] = from_f<T>(acc[i][q]);
-      else
-        dA[int64_t(pcol + jj) * d_in + d] = from_f<T>(acc[i][q]);
+      const T g = from_f<T>(acc[i][q]);
+      if (is_dB) {
+        dB[int64_t(d) * R + pcol + jj] = g;
+        if (B_upd) sgd_apply(B_upd + int64_t(d) * R + pcol + jj, g, lr);  // fused SGD step
+      } else {
+        dA[int64_t(pcol + jj) * d_in + d] = g;
+        if (A_upd) sgd_apply(A_upd + int64_t(pcol + jj) * d_in + d, g, lr);
+      }
     }
   }
 }
@@ -274,9 +278,11 @@ int launch_backward(const SimtCall& a, cudaStream_t st) {
   void* dA = (a.bwd_stages & MLORA_BWD_DA) ? a.dA : nullptr;
   void* dB = (a.bwd_stages & MLORA_BWD_DB) && a.db1 > a.db0 ? a.dB : nullptr;
   if (a.n_reduce > 0 && (dA || dB)) {
+    T* A_upd = dA && (a.bwd_stages & MLORA_BWD_SGD_A) ? (T*)a.A_pack : nullptr;
+    T* B_upd = dB && (a.bwd_stages & MLORA_BWD_SGD_B) ? (T*)a.B_pack : nullptr;
     k_reduce<T><<<dim3(a.n_reduce, kMaxChunksPerItem, 2), NT, 0, st>>>(
         a.plan, (const T*)a.X, (const T*)a.dY, (const T*)a.zsave, (const T*)a.dzt, (T*)dA,
-        (T*)dB, a.M, a.d_in, a.d_out, a.R, a.db0, a.db1);
+        (T*)dB, a.M, a.d_in, a.d_out, a.R, a.db0, a.db1, A_upd, B_upd, a.lr);
     count_launch();
   }
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;

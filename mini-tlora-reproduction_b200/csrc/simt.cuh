@@ -24,6 +24,7 @@ struct SimtCall {
   // backward stages (MLORA_BWD_*) and dB block range (128-row blocks of d_out)
   int bwd_stages = MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB;
   int db0 = 0, db1 = 0;
+  float lr = 0.f;  // fused SGD step (MLORA_BWD_SGD_A / _B)
 };
 
 int simt_forward(const SimtCall& a, cudaStream_t st);

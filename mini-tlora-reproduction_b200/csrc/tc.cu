@@ -117,6 +117,11 @@ struct TcParams {
   __nv_bfloat16* out;  // Y, dX, Zt or dZt
   __nv_bfloat16* dA;
   __nv_bfloat16* dB;
+  // reduce with the fused SGD step: A_pack / B_pack updated from the stored
+  // gradients (nullptr = no update)
+  __nv_bfloat16* A_upd;
+  __nv_bfloat16* B_upd;
+  float lr;
   // forward main with the peer all-reduce: partial tiles go to their owner
   // rank's receive buffer (slot ar_rank) instead of Y
   int ar_on, ar_rank, ar_world, ar_lt_stride;
@@ -369,6 +374,12 @@ __device__ __forceinline__ void st1(__nv_bfloat16* dst, float v, bool f16) {
 __device__ __forceinline__ float ld1(const __nv_bfloat16* src, bool f16) {
   const unsigned short b = *reinterpret_cast<const unsigned short*>(src);
   return f16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+}
+// P <- P - lr G for one element, G = v as stored in 16 bits (the fused SGD
+// step; the same expression as the separate SGD pass)
+__device__ __forceinline__ void sgd1(__nv_bfloat16* P, float v, float lr, bool f16) {
+  const float g = f16 ? __half2float(__float2half_rn(v)) : __bfloat162float(__float2bfloat16_rn(v));
+  st1(P, ld1(P, f16) - lr * g, f16);
 }
 __device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&f)[32], bool f16) {
   uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -937,12 +948,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
                 for (int q = 0; q < 32; ++q)
                   if (col + q < rvalid) st1(dst + q, __uint_as_float(v[q]), p.f16);
               }
+              if (p.B_upd) {  // fused SGD step on the same elements of B_pack
+                __nv_bfloat16* P = p.B_upd + int64_t(d) * p.R + pcol + col;
+#pragma unroll
+                for (int q = 0; q < 32; ++q)
+                  if (col + q < rvalid) sgd1(P + q, __uint_as_float(v[q]), p.lr, p.f16);
+              }
             } else {
               if (d >= p.d_in) continue;
 #pragma unroll
               for (int q = 0; q < 32; ++q)
-                if (col + q < rvalid)
-                  st1(p.dA + int64_t(pcol + col + q) * p.d_in + d, __uint_as_float(v[q]), p.f16);
+                if (col + q < rvalid) {
+                  const int64_t e = int64_t(pcol + col + q) * p.d_in + d;
+                  st1(p.dA + e, __uint_as_float(v[q]), p.f16);
+                  if (p.A_upd) sgd1(p.A_upd + e, __uint_as_float(v[q]), p.lr, p.f16);  // fused SGD step
+                }
             }
           }
         }
@@ -1507,6 +1527,11 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.da_on = da ? 1 : 0;
     prm.db0 = db ? a.db0 : 0;
     prm.db1 = db ? a.db1 : 0;
+    prm.A_upd = da && (a.bwd_stages & MLORA_BWD_SGD_A)
+                    ? reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.A_pack)) : nullptr;
+    prm.B_upd = db && (a.bwd_stages & MLORA_BWD_SGD_B)
+                    ? reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.B_pack)) : nullptr;
+    prm.lr = a.lr;
     int nc = 1;
     for (const ReduceItem& r : a.host->reduce) nc = std::max(nc, int(r.nc));
     set_ring(prm, kA1Bytes, nc * kBox64);  // A: two 64x64 boxes

@@ -26,6 +26,7 @@ struct TcCall {
   // backward stages (MLORA_BWD_*), dZ tile range [t0, t1) and dB block range
   int bwd_stages = MLORA_BWD_DZ | MLORA_BWD_DX | MLORA_BWD_DA | MLORA_BWD_DB;
   int db0 = 0, db1 = 0;
+  float lr = 0.f;  // fused SGD step (MLORA_BWD_SGD_A / _B in bwd_stages)
   bool pair_fwd = false;  // forward mainloop on 2-SM pairs (tcgen05 cta_group::2)
   bool pair_dx = true;    // dX mainloop on 2-SM pairs
   // forward MAIN: push the partial tiles to their owner ranks (mlora_forward_push)

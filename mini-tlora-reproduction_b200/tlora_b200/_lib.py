@@ -41,6 +41,9 @@ BWD_DZ = 1
 BWD_DX = 2
 BWD_DA = 4
 BWD_DB = 8
+BWD_SGD_A = 16
+BWD_SGD_B = 32
+FUSED_SGD = 2  # mlora_problem.flags
 
 IMPL_AUTO = 0
 IMPL_SIMT = 1
@@ -62,6 +65,7 @@ class Problem(ctypes.Structure):
         ("max_ctas", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("err_word", ctypes.c_void_p),  # device int32 of this call's flags, or NULL (library-wide word)
+        ("lr", ctypes.c_float),          # learning rate of the fused SGD step
     ]
 
 

@@ -453,10 +453,29 @@ class StagedBackward:
     def run_db(self, b0=0, b1=None):
         self._run(_lib.BWD_DB, 0, 0, b0, self.n_db if b1 is None else b1)
 
-    def run_all(self):
+    def _run_sgd(self, stages, lr, t0=0, t1=0, b0=0, b1=0):
+        """A call whose reduction also applies the isolated SGD step (the
+        MLORA_BWD_SGD_* stages) with learning rate ``lr``."""
+        self.args.prob.lr = float(lr)
+        try:
+            self._run(stages, t0, t1, b0, b1)
+        finally:
+            self.args.prob.lr = 0.0
+
+    def run_all(self, sgd_lr: Optional[float] = None):
         """Every stage over all tiles in one call (dZ, then the dX mainloop
-        overlapping its tail, then dA and dB in one reduction launch)."""
-        self._run(_lib.BWD_DZ | _lib.BWD_DX | _lib.BWD_DA | _lib.BWD_DB, 0, self.n_tiles, 0, self.n_db)
+        overlapping its tail, then dA and dB in one reduction launch); with
+        ``sgd_lr`` the reduction's epilogue also applies the isolated SGD step
+        to A_pack and B_pack (every adapter that owns rows)."""
+        stages = _lib.BWD_DZ | _lib.BWD_DX | _lib.BWD_DA | _lib.BWD_DB
+        if sgd_lr is None:
+            self._run(stages, 0, self.n_tiles, 0, self.n_db)
+        else:
+            self._run_sgd(stages | _lib.BWD_SGD_A | _lib.BWD_SGD_B, sgd_lr, 0, self.n_tiles, 0, self.n_db)
+
+    def run_da_sgd(self, lr: float):
+        """dA with the SGD step of A_pack fused into its reduction."""
+        self._run_sgd(_lib.BWD_DA | _lib.BWD_SGD_A, lr)
 
     def run_dadb(self, b0=0, b1=None):
         """dA and dB (d_out blocks [b0, b1)) in one reduction launch."""

@@ -100,6 +100,8 @@ def _share(total: int, rank: int, world: int) -> Tuple[int, int]:
 
 class NativeCompute:
     """The native kernels (tcgen05 for bf16) behind the sharded layer.  The
+    isolated SGD step of A (and, with one rank, of B) is fused into the
+    gradient reduction's epilogue (``fused_sgd``).  The
     staged forward / backward objects (call arguments, buffers, the routing
     plan kept resident in a device workspace) are built once per input
     buffer and plan and reused by every later step, so a step's host work is
@@ -107,6 +109,8 @@ class NativeCompute:
     that run beside the all-reduces; the kernels hand out work items
     dynamically, so CTAs that find their SM taken simply start later and take
     fewer items, and 0 (no reservation) is the measured best on B200."""
+
+    fused_sgd = True
 
     def __init__(self, impl: str = "auto", comm_sms: int = 0):
         self.impl = impl
@@ -178,8 +182,11 @@ class NativeCompute:
     def bwd_dx(self, b):
         b["bw"].run_dx()
 
-    def bwd_da(self, b):
-        b["bw"].run_da()
+    def bwd_da(self, b, sgd_lr=None):
+        if sgd_lr is None:
+            b["bw"].run_da()
+        else:
+            b["bw"].run_da_sgd(sgd_lr)
 
     def bwd_db(self, b, b0, b1):
         b["bw"].run_db(b0, b1)
@@ -187,14 +194,18 @@ class NativeCompute:
     def bwd_dadb(self, b):
         b["bw"].run_dadb()
 
-    def bwd_all(self, b):
-        b["bw"].run_all()
+    def bwd_all(self, b, sgd_lr=None):
+        b["bw"].run_all(sgd_lr)
 
-    def sgd(self, layer, plan, dA_p, dB, lr):
-        """Isolated SGD of the plan's active adapters, one launch; the item
-        list (pointers into the layer's weights and the reused gradient
-        buffers) is built once per plan and buffers."""
-        key = (id(plan), layer.A_pack.data_ptr(), layer.B_pack.data_ptr(), dA_p.data_ptr(), dB.data_ptr())
+    def sgd(self, layer, plan, dA_p, dB, lr, which=("A", "B")):
+        """Isolated SGD of the plan's active adapters (their A and / or B, as
+        ``which`` lists), one launch; the item list (pointers into the layer's
+        weights and the reused gradient buffers) is built once per plan and
+        buffers."""
+        which = tuple(which)
+        if not which:
+            return 0
+        key = (id(plan), which, layer.A_pack.data_ptr(), layer.B_pack.data_ptr(), dA_p.data_ptr(), dB.data_ptr())
         c = getattr(self, "_sgd", None)
         if c is None or c[0] != key:
             pairs = []
@@ -202,8 +213,10 @@ class NativeCompute:
                 if not plan.active[i]:
                     continue
                 o, r = int(layer.table.pack_off[i]), int(layer.table.rank[i])
-                pairs.append((layer.A_pack[o:o + r], dA_p[o:o + r]))
-                pairs.append((layer.B_pack[:, o:o + r], dB[:, o:o + r]))
+                if "A" in which:
+                    pairs.append((layer.A_pack[o:o + r], dA_p[o:o + r]))
+                if "B" in which:
+                    pairs.append((layer.B_pack[:, o:o + r], dB[:, o:o + r]))
             c = self._sgd = (key, ops.SgdItems(pairs), plan)
         return c[1].step(lr)
 
@@ -454,27 +467,35 @@ class ShardedLayer:
         self._pending = None
 
     # -- backward and the step ---------------------------------------------------
-    def backward(self, ctx, x_p, dy, overlapped=False, after_dz=None):
+    def backward(self, ctx, x_p, dy, overlapped=False, after_dz=None, lr=None):
         """Backward on this rank's shard.  dZ (needs all of dY and B) and dB
         (needs all of dY and Z) are split across ranks — dZ by tiles, dB by
         128-row blocks of d_out — and summed with two small async all-reduces:
         dZ's runs beside this rank's dB share, dB's beside the dX mainloop.
-        dX_p and dA_p are local.  Returns (dX_p, dA_p, dB, dB work handle or
-        None: wait for it before reading dB)."""
+        dX_p and dA_p are local.  With ``lr`` and a compute that fuses the SGD
+        step, the reductions also update the weights whose gradients are
+        complete on this rank (A_p; with one rank also B).  Returns (dX_p,
+        dA_p, dB, dB work handle or None: wait for it before reading dB, the
+        weights already updated: a subset of {"A", "B"})."""
         c = self.compute
         coll = self.world > 1
+        fused = lr if (lr is not None and getattr(c, "fused_sgd", False)) else None
         b = c.bwd_begin(ctx, self, x_p, dy, overlapped, partial=coll)
         if not coll:
             if after_dz is not None:
                 after_dz()
             if hasattr(c, "bwd_all"):
-                c.bwd_all(b)  # dZ, dX (overlapping dZ's tail), dA and dB in one call
+                # dZ, dX (overlapping dZ's tail), dA and dB in one call, the
+                # SGD step in the reduction's epilogue
+                c.bwd_all(b, sgd_lr=fused)
+                applied = ("A", "B") if fused is not None else ()
             else:
                 c.bwd_dz(b, 0, b["n_tiles"])
                 c.bwd_dx(b)
                 c.bwd_dadb(b)
+                applied = ()
             self._mark("bwd")
-            return b["dx"], b["dA"], b["dB"], None
+            return b["dx"], b["dA"], b["dB"], None, applied
         t0, t1 = _share(b["n_tiles"], self.rank, self.world)
         c.bwd_dz(b, t0, t1)
         self._mark("bwd_dz")
@@ -492,9 +513,14 @@ class ShardedLayer:
             after_dz()
         c.bwd_dx(b)
         self._mark("bwd_dx")
-        c.bwd_da(b)
+        if fused is not None:
+            c.bwd_da(b, sgd_lr=fused)  # dA_p is complete on this rank: its SGD step in the epilogue
+            applied = ("A",)
+        else:
+            c.bwd_da(b)
+            applied = ()
         self._mark("bwd_da")
-        return b["dx"], b["dA"], b["dB"], hdb
+        return b["dx"], b["dA"], b["dB"], hdb, applied
 
     def step(self, x_p, plan, dy, n_nano: int, lr: float, pipelined: bool = True, comm: bool = True):
         """Forward, backward and isolated SGD on this rank's shard.  Returns
@@ -515,13 +541,16 @@ class ShardedLayer:
                     w.launch()
 
         with _Range("mlora.backward"):
-            dx_p, dA_p, dB, hdb = self.backward(ctx, x_p, dy, overlapped=bool(works), after_dz=after_dz)
+            dx_p, dA_p, dB, hdb, applied = self.backward(ctx, x_p, dy, overlapped=bool(works), after_dz=after_dz,
+                                                         lr=lr)
         if hdb is not None:
             hdb.wait()
         self._mark("bwd_db_allreduce")
-        with _Range("mlora.sgd"):
-            self.compute.sgd(self, plan, dA_p, dB, lr)
-        self._mark("sgd")
+        rest = tuple(w for w in ("A", "B") if w not in applied)
+        if rest:
+            with _Range("mlora.sgd"):
+                self.compute.sgd(self, plan, dA_p, dB, lr, which=rest)
+            self._mark("sgd")
         for w in works:
             w.wait()
         self._mark("end")

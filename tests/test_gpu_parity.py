@@ -430,6 +430,78 @@ def test_per_call_error_words_on_two_streams(impl):
     assert torch.equal(ys[1], y_ref)
 
 
+@pytest.mark.parametrize("impl", ["tc", "tc2", "simt"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_sgd_equals_separate_sgd(impl, dtype):
+    """The isolated SGD step fused into the dA / dB reduction's epilogue
+    (MLORA_BWD_SGD_A | MLORA_BWD_SGD_B, and MLORA_FUSED_SGD of mlora_backward)
+    writes the same gradients and leaves A_pack / B_pack bit-identical to the
+    backward followed by the separate SGD pass (mlora_sgd); adapters that own
+    no rows are neither read nor written (phase5d_triton_training.py:554-559)."""
+    import ctypes
+    from tlora_b200 import ops, _lib
+    m = _edge_module(320, 272, {0: 8, 1: 100, 2: 3, 3: 64}, dtype)
+    ids = torch.tensor([0] * 300 + [1] * 129 + [3] * 40, dtype=torch.int64)  # adapter 2 owns no rows
+    x = torch.randn(ids.shape[0], 320, device=DEV).to(dtype)
+    dy = torch.randn(ids.shape[0], 272, device=DEV).to(dtype)
+    A_pack, B_pack, table = m.packed()
+    plan = ops.route(ids, table, torch.device(DEV))
+    sc = np.array([1.5, 0.5, 2.0, 1.0], np.float32)
+    lr = 0.25
+    A0, B0 = A_pack.clone(), B_pack.clone()
+    st = ops.LayerState(table, sc, plan, A_pack, B_pack, impl)
+    fw = ops.StagedForward(x, m.base.weight, m.base.bias, st)
+    fw.shrink_main()
+    bw = ops.StagedBackward(dy, x, m.base.weight, fw.z, st)
+    bw.run_all()
+    pairs = []
+    for i in range(table.n):
+        if plan.active[i]:
+            o, r = int(table.pack_off[i]), int(table.rank[i])
+            pairs += [(A_pack[o:o + r], bw.dA[o:o + r]), (B_pack[:, o:o + r], bw.dB[:, o:o + r])]
+    ops.sgd_step_(pairs, lr)
+    want = [t.clone() for t in (bw.dA, bw.dB, bw.dx, A_pack, B_pack)]
+    # fused, staged call
+    with torch.no_grad():
+        A_pack.copy_(A0)
+        B_pack.copy_(B0)
+    bw2 = ops.StagedBackward(dy, x, m.base.weight, fw.z, st)
+    bw2.run_all(sgd_lr=lr)
+    torch.cuda.synchronize()
+    for name, a, b in zip(("dA", "dB", "dX", "A", "B"), (bw2.dA, bw2.dB, bw2.dx, A_pack, B_pack), want):
+        if name in ("dA", "dB"):  # rows / columns of adapter 2 are never written
+            o, r = int(table.pack_off[2]), int(table.rank[2])
+            keep = torch.ones_like(a, dtype=torch.bool)
+            if name == "dA":
+                keep[o:o + r] = False
+            else:
+                keep[:, o:o + r] = False
+            a, b = a[keep], b[keep]
+        assert torch.equal(a, b), name
+    o, r = int(table.pack_off[2]), int(table.rank[2])
+    assert torch.equal(A_pack[o:o + r], A0[o:o + r]) and torch.equal(B_pack[:, o:o + r], B0[:, o:o + r])
+    assert not torch.equal(A_pack, A0) and not torch.equal(B_pack, B0)
+    # fused through mlora_backward's MLORA_FUSED_SGD flag
+    with torch.no_grad():
+        A_pack.copy_(A0)
+        B_pack.copy_(B0)
+    args = ops._CallArgs(ids.shape[0], 320, 272, ops.mlora_dtype(dtype), impl, plan, table, sc)
+    _, wb = args.sizes()
+    ws = torch.empty(wb, dtype=torch.uint8, device=DEV)
+    dA = torch.zeros_like(A_pack)
+    dB = torch.zeros_like(B_pack)
+    args.prob.flags = _lib.FUSED_SGD
+    args.prob.lr = lr
+    _lib.call("mlora_backward", ctypes.byref(args.prob), ctypes.byref(args.route), ctypes.c_void_p(dy.data_ptr()),
+              ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(m.base.weight.data_ptr()),
+              ctypes.c_void_p(A_pack.data_ptr()), ctypes.c_void_p(B_pack.data_ptr()),
+              ctypes.c_void_p(fw.z.data_ptr()), None, ctypes.c_void_p(dA.data_ptr()),
+              ctypes.c_void_p(dB.data_ptr()), ctypes.c_void_p(ws.data_ptr()), wb,
+              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(A_pack, want[3]) and torch.equal(B_pack, want[4])
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_gather_scatter_rows_round_trip(dtype):
     """mlora_gather_rows / mlora_scatter_rows (the C ABI's row permutation for

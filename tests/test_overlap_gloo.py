@@ -87,12 +87,14 @@ class DenseCompute:
         self.bwd_da(b)
         self.bwd_db(b, 0, b["n_db"])
 
-    def sgd(self, layer, plan, dA, dB, lr):
+    def sgd(self, layer, plan, dA, dB, lr, which=("A", "B")):
         for i in range(layer.table.n):
             if plan.active[i]:
                 o, r = int(layer.table.pack_off[i]), int(layer.table.rank[i])
-                layer.A_pack[o:o + r] -= lr * dA[o:o + r]
-                layer.B_pack[:, o:o + r] -= lr * dB[:, o:o + r]
+                if "A" in which:
+                    layer.A_pack[o:o + r] -= lr * dA[o:o + r]
+                if "B" in which:
+                    layer.B_pack[:, o:o + r] -= lr * dB[:, o:o + r]
 
 
 def _free_port():
