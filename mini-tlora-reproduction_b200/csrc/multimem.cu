@@ -49,7 +49,7 @@ namespace mlora {
 namespace {
 
 constexpr int kMcThreads = 512;
-constexpr int kMcUnroll = 4;  // 16-byte units in flight per thread
+constexpr int kMcUnroll = 8;  // 16-byte units in flight per thread
 constexpr unsigned long long kMcDefaultTimeoutNs = 2000000000ull;
 // flag words: ready[s] at s, done[s] at MLORA_MC_SLOTS + s, and, used through
 // this rank's own copy only, the CTA counter of the rank's reduce launch of
