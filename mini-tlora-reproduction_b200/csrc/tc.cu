@@ -279,7 +279,6 @@ __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.w
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_3() { asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -339,32 +338,6 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// tcgen05.ld of 32 columns without the wait: the registers are defined only
-// after tc_ld32_wait, which names them as operands so that the compiler keeps
-// every use of them after the wait
-__device__ __forceinline__ void tc_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tc_ld32_wait(uint32_t (&r)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
-                 "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
-                 "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
-                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-               :
-               : "memory");
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
@@ -633,48 +606,40 @@ __device__ __forceinline__ void ar_arrive(const TcParams& p, int tile, int lane)
   }
 }
 
-// The bias of one 256-column N block, spread over the warp: lane l holds
-// columns n0 + 8l .. n0 + 8l + 7 (one 16-byte load per lane, issued once per
-// work item; zero past the end of the row, where nothing is stored).
-__device__ __forceinline__ uint4 bias_block(const TcParams& p, int n0, int lane) {
-  uint4 u = make_uint4(0u, 0u, 0u, 0u);
-  const int c = n0 + 8 * lane;
-  if (!p.bias || c >= p.d_out) return u;
-  if (c + 8 <= p.d_out) return __ldg(reinterpret_cast<const uint4*>(p.bias + c));  // 16-byte aligned
-  const unsigned short* b16 = reinterpret_cast<const unsigned short*>(p.bias);
-  uint32_t h[8];
+template <int MODE, int NBUF>
+__device__ __forceinline__ void epi_main_slice(const TcParams& p, int64_t row_w0, int n0, int col, bool empty_acc,
+                                               uint32_t taddr, uint32_t buf, int lane) {
+  const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
+  float f[32];
+  if (!empty_acc) {
+    uint32_t v[32];
+    tc_ld32(taddr, v);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) h[e] = c + e < p.d_out ? uint32_t(b16[c + e]) : 0u;
-  return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
-}
-
-// f += bias of slice columns [col, col + 32), held by lanes col/8 .. col/8 + 3
-__device__ __forceinline__ void add_bias_slice(float (&f)[32], const uint4 bias, int col, bool f16) {
+    for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
+  } else {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int src = (col >> 3) + q;
-    const uint32_t w[4] = {__shfl_sync(0xffffffffu, bias.x, src), __shfl_sync(0xffffffffu, bias.y, src),
-                           __shfl_sync(0xffffffffu, bias.z, src), __shfl_sync(0xffffffffu, bias.w, src)};
+    for (int q = 0; q < 32; ++q) f[q] = 0.f;
+  }
+  if (MODE == FWD_MAIN && p.bias) {
+    if (n0 + col + 32 <= N) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + col);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 h = unpack2(w[e], f16);
-      f[8 * q + 2 * e] += h.x;
-      f[8 * q + 2 * e + 1] += h.y;
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(b4 + q);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 h = unpack2(w[e], p.f16);
+          f[8 * q + 2 * e] += h.x;
+          f[8 * q + 2 * e + 1] += h.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q)
+        if (n0 + col + q < N) f[q] += ld1(p.bias + n0 + col + q, p.f16);
     }
   }
-}
-
-// Store one 32x32 slice of an output tile (rows row_w0.., columns n0 + col..)
-// from f: to the owner rank (peer all-reduce), straight to the caller's row
-// order (out_rows), or staged in shared memory and written by a TMA store.
-// The warp's staging buffers rotate: `slot` counts the warp's staged slices,
-// and the store issued from a buffer `nbuf` slices ago must have finished
-// reading it before it is rewritten.
-template <int MODE>
-__device__ __forceinline__ void out_slice(const TcParams& p, int64_t row_w0, int n0, int col, const float (&f)[32],
-                                          const uint32_t (&bufs)[4], int nbuf, uint32_t& slot, int lane) {
-  const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-  const uint32_t buf = bufs[slot % uint32_t(nbuf)];
   if (MODE == FWD_MAIN && p.ar_on) {
     ar_push_box(p, row_w0, n0, col, f, buf, lane);
     return;
@@ -697,10 +662,9 @@ __device__ __forceinline__ void out_slice(const TcParams& p, int64_t row_w0, int
     }
     return;
   }
-  if (lane == 0) {  // the store issued from this buffer nbuf slices ago has read it
-    if (nbuf >= 4) bulk_wait_read_3();
-    else if (nbuf == 2) bulk_wait_read_1();
-    else bulk_wait_read_0();
+  if (lane == 0) {
+    if (NBUF == 2) bulk_wait_read_1();  // the store issued from this buffer two slices ago
+    else bulk_wait_read_0();            // the store issued from this buffer one slice ago
   }
   __syncwarp();
   // row `lane` of the 32x32 box: 64 bytes, 16-byte chunk q at q ^ ((lane >> 1) & 3)
@@ -716,38 +680,6 @@ __device__ __forceinline__ void out_slice(const TcParams& p, int64_t row_w0, int
   if (lane == 0) {
     if (row_w0 < p.M) tma_store(&p.mY, buf, n0 + col, int(row_w0));
     bulk_commit();
-  }
-  ++slot;
-}
-
-// One work item's epilogue for the warp's 32 accumulator rows (TMEM lanes):
-// the 32-column slices of the accumulator at `tbase` -> registers (the next
-// slice's TMEM load issued while this one is stored) -> + bias (loaded once
-// for the item) -> out_slice.  Warp-collective.
-template <int MODE>
-__device__ __forceinline__ void epi_main_item(const TcParams& p, int64_t row_w0, int n0, bool empty_acc,
-                                              uint32_t tbase, const uint32_t (&bufs)[4], int nbuf, uint32_t& slot,
-                                              int lane) {
-  const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
-  const int ncols = min(kAccCols, N - n0);  // columns of the block inside the output
-  const bool has_bias = MODE == FWD_MAIN && p.bias != nullptr;
-  uint4 bias = make_uint4(0u, 0u, 0u, 0u);
-  if (has_bias) bias = bias_block(p, n0, lane);
-  uint32_t v[32];
-  if (!empty_acc && ncols > 0) tc_ld32_issue(tbase, v);
-  for (int col = 0; col < ncols; col += 32) {
-    float f[32];
-    if (!empty_acc) {
-      tc_ld32_wait(v);
-#pragma unroll
-      for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
-      if (col + 32 < ncols) tc_ld32_issue(tbase + col + 32, v);  // overlaps this slice's stores
-    } else {
-#pragma unroll
-      for (int q = 0; q < 32; ++q) f[q] = 0.f;
-    }
-    if (has_bias) add_bias_slice(f, bias, col, p.f16);
-    out_slice<MODE>(p, row_w0, n0, col, f, bufs, nbuf, slot, lane);
   }
 }
 
@@ -954,23 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
     const int r = quad * 32 + lane;  // accumulator row = TMEM lane
-    // staging buffers of this warp: one beside the ring, and up to three more in
-    // the ring's unused tail (a mainloop's 4 stages of 48 KB leave 24 KB)
-    uint32_t bufs[4];
-    int nbuf = 1;
-    bufs[0] = su32(stage_out) + uint32_t(warp - 2) * 2048u;
-    {
-      const uint32_t tail = uint32_t(n_stages * stage_bytes);
-      const int spare = int((uint32_t(kRing1Bytes) - tail) / (4u * 2048u));
-      for (int b = 1; b < 4; ++b) {
-        bufs[b] = bufs[0];
-        if (b <= spare) {
-          bufs[b] = su32(smem) + tail + uint32_t(((b - 1) * 4 + (warp - 2)) * 2048);
-          nbuf = b + 1;
-        }
-      }
-    }
-    uint32_t slot = 0;
+    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 2048u;
     int acc = 0;
     uint32_t acc_phase = 0;
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
@@ -991,8 +907,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
         const int64_t row_w0 = int64_t(it.t) * kTileRows + it.half * kHalfRows + quad * 32;
         const int n0 = it.nb * 256;
         const bool empty_acc = it.nk == 0;  // delta-only call on a tile without LoRA rows
-        (void)N;
-        epi_main_item<MODE>(p, row_w0, n0, empty_acc, tbase, bufs, nbuf, slot, lane);
+        for (int col = 0; col < kAccCols; col += 32) {
+          if (n0 + col >= N) break;
+          epi_main_slice<MODE, 1>(p, row_w0, n0, col, empty_acc, tbase + col, obuf, lane);
+        }
       } else if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
         const int rt = it.half * kHalfRows + r;  // row inside the 256-row tile
         for (int i = 0; i < it.nc; ++i) {
@@ -1249,8 +1167,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     const int quad = warp % 4;
     const uint32_t tempty_even0 = mapa(su32(&tempty[0]), 0), tempty_even1 = mapa(su32(&tempty[1]), 0);
     const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 4096u;
-    const uint32_t bufs[4] = {obuf, obuf + 2048u, obuf, obuf + 2048u};
-    uint32_t slot = 0;
+    uint32_t slices = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
@@ -1273,8 +1190,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       const int64_t row_w0 = int64_t(it.t) * kTileRows + int(crank) * kHalfRows + quad * 32;
       const int n0 = it.nb * 256;
       const bool empty_acc = it.nk == 0;
-      (void)N;
-      epi_main_item<MODE>(p, row_w0, n0, empty_acc, tbase, bufs, 2, slot, lane);
+      for (int col = 0; col < kAccCols; col += 32) {
+        if (n0 + col >= N) break;
+        epi_main_slice<MODE, 2>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
+        ++slices;
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_even1 : tempty_even0);  // one remote arrival per warp
