@@ -1323,7 +1323,14 @@ int launch1(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   if (sms <= 0) return MLORA_ERR_CUDA;
   MLORA_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(&k_tc<MODE>), kSmem1));
   prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
-  const int grid = prm.n_items < sms ? prm.n_items : sms;
+  int grid = prm.n_items < sms ? prm.n_items : sms;
+  if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) {
+    // HBM-bound roles with equal items: as many CTAs as balance the waves
+    // (306 items on 148 SMs: 102 CTAs of 3 items, no 10-item last wave); the
+    // fewer SMs still keep enough bytes in flight to saturate HBM
+    const int waves = (prm.n_items + sms - 1) / sms;
+    grid = (prm.n_items + waves - 1) / waves;
+  }
   cudaEvent_t ev[2] = {nullptr, nullptr};
   const bool timed = timing_begin(st, ev);
   if (timed || !pdl_enabled()) pdl = false;  // events between the launches order them anyway
