@@ -79,6 +79,7 @@ extern "C" {
                                SMs, dX mainloop on 2-SM pairs (the faster variant of each, measured) */
 #define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with both mainloops on single SMs (comparison path) */
 #define MLORA_IMPL_TC_2SM 4 /* as MLORA_IMPL_TC with both mainloops on 2-SM pairs (comparison path) */
+#define MLORA_IMPL_TC_WIDE 5 /* as MLORA_IMPL_TC_2SM with 256 x 512 pair tiles (comparison path) */
 
 typedef struct mlora_problem {
   int64_t rows;   /* M: rows of X in this call */

@@ -101,7 +101,8 @@ int choose_impl(const mlora_problem* prob, std::initializer_list<const void*> pt
   if (!pointers_aligned(ptrs, size_t(elem_bytes(prob->dtype)))) return -1;
   const bool tc_ok = tc_shape_ok(prob) && pointers_aligned(ptrs, 16);
   if (prob->impl == MLORA_IMPL_SIMT) return MLORA_IMPL_SIMT;
-  if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM || prob->impl == MLORA_IMPL_TC_2SM)
+  if (prob->impl == MLORA_IMPL_TC || prob->impl == MLORA_IMPL_TC_1SM || prob->impl == MLORA_IMPL_TC_2SM ||
+      prob->impl == MLORA_IMPL_TC_WIDE)
     return tc_ok ? MLORA_IMPL_TC : -1;
   if (prob->impl != MLORA_IMPL_AUTO) return -1;
   return (tc_ok && tc_available()) ? MLORA_IMPL_TC : MLORA_IMPL_SIMT;
@@ -188,7 +189,8 @@ int forward_staged(const mlora_problem* prob, const mlora_routing* route, const 
     a.Y = Y; a.zsave = zsave; a.out_rows = route->out_rows;
     a.stages = stages; a.t0 = tile_begin; a.t1 = tile_end;
     a.max_ctas = prob->max_ctas;
-    a.pair_fwd = prob->impl == MLORA_IMPL_TC_2SM;
+    a.pair_fwd = prob->impl == MLORA_IMPL_TC_2SM || prob->impl == MLORA_IMPL_TC_WIDE;
+    a.wide = prob->impl == MLORA_IMPL_TC_WIDE;
     return tc_forward(a, s);
   }
   SimtCall a;
@@ -289,6 +291,7 @@ extern "C" int mlora_backward_staged(const mlora_problem* prob, const mlora_rout
     a.out_rows = route->out_rows;
     a.max_ctas = prob->max_ctas;
     a.pair_dx = prob->impl != MLORA_IMPL_TC_1SM;
+    a.wide = prob->impl == MLORA_IMPL_TC_WIDE;
     a.bwd_stages = stages; a.t0 = tile_begin; a.t1 = tile_end; a.db0 = db_begin; a.db1 = db_end;
     a.lr = prob->lr;
     return tc_backward(a, s);

@@ -30,6 +30,10 @@
 //    barrier, the even CTA issues the MMAs and its commits signal the barriers
 //    of both CTAs.  Per SM this moves 2/3 of the operand bytes of a 1-SM
 //    128x256 tile for the same MMA work.
+//  * k_tc2w (FWD_MAIN, DX_MAIN, selected by MLORA_IMPL_TC_WIDE): the pair on
+//    a 256x512 tile, two M = 256, N = 256 MMAs per k-block into one
+//    512-column accumulator drained in two halves (48 KB per stage, 4
+//    stages); bit-identical to k_tc2, a comparison path.
 //  * k_tc (SHRINK_*, REDUCE, and the 1-SM variant of the mainloops): one CTA,
 //    M = 128, N <= 256, a 216 KB ring cut per launch (4 stages of 48 KB for a
 //    mainloop, up to 9 narrower stages for the HBM-bound roles).
@@ -85,7 +89,13 @@ constexpr int kStages2 = 6;
 constexpr int kA2Bytes = 128 * 64 * 2;
 constexpr int kStage2Bytes = kA2Bytes + 128 * 64 * 2;
 constexpr int kSmem2 = kStages2 * kStage2Bytes + kStageOut2Bytes + 1024 + 512;
-static_assert(kSmem1 <= 232448 && kSmem2 <= 232448, "dynamic shared memory above 227 KB");
+// wide 2-SM kernel: per CTA A 128x64 (16 KB) + the CTA's 128 columns of each of
+// the two 256-wide N halves (2 x 16 KB) per stage
+constexpr int kStagesW = 4;
+constexpr int kBHalfBytes = 128 * 64 * 2;
+constexpr int kStageWBytes = kA2Bytes + 2 * kBHalfBytes;
+constexpr int kSmemW = kStagesW * kStageWBytes + kStageOut2Bytes + 1024 + 512;
+static_assert(kSmem1 <= 232448 && kSmem2 <= 232448 && kSmemW <= 232448, "dynamic shared memory above 227 KB");
 
 enum Mode { FWD_MAIN = 0, DX_MAIN = 1, SHRINK_FWD = 2, SHRINK_BWD = 3, REDUCE = 4 };
 
@@ -100,7 +110,8 @@ struct TcParams {
   int tile0;        // main: first plan tile of the launch
   int n_tiles_rng;  // main: plan tiles of the launch
   int no_expand;    // main: leave the LoRA expand out
-  int n_nblk;       // main: 256-wide N blocks
+  int n_nblk;       // main: 256-wide N blocks (the peer all-reduce's block layout)
+  int n_rblk;       // main: N blocks of the raster (256 wide, 512 in the wide pair kernel)
   int raster_n;     // main: 0 = groups of M tiles sweep all N blocks, 1 = groups of N blocks sweep all M
   int group;        // main: tiles (raster_n = 0) or N blocks (raster_n = 1) per raster group
   int nk_main;      // main / shrink: 64-wide K blocks of the dense part
@@ -411,7 +422,7 @@ __device__ __forceinline__ void raster(const TcParams& p, int item, int units, I
   int u;
   if (!p.raster_n) {
     const int gm = p.group * units;
-    const int per_group = gm * p.n_nblk;
+    const int per_group = gm * p.n_rblk;
     const int g = item / per_group, r = item % per_group;
     const int u0 = g * gm;
     const int gs = min(gm, n_units - u0);
@@ -421,7 +432,7 @@ __device__ __forceinline__ void raster(const TcParams& p, int item, int units, I
     const int per_group = p.group * n_units;
     const int g = item / per_group, r = item % per_group;
     const int n0 = g * p.group;
-    const int gs = min(p.group, p.n_nblk - n0);
+    const int gs = min(p.group, p.n_rblk - n0);
     u = r / gs;
     it.nb = n0 + r % gs;
   }
@@ -1214,6 +1225,272 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
   }
 }
 
+// ------------------------------------------------------------------ 2-SM wide kernel
+// A cluster of two CTAs per 256 x 512 output tile of FWD_MAIN / DX_MAIN.  Each
+// k-block, two tcgen05.mma.cta_group::2 (M = 256, N = 256) share the A tile
+// and write the two 256-column halves of ONE 512-column TMEM accumulator per
+// CTA.  CTA r stages rows [128 r, 128 r + 128) of the A tile and, of each
+// 256-wide N half, its own 128 columns: 48 KB of TMA writes into each SM's
+// shared memory per 1024 MMA cycles, against 32 KB per 512 cycles for the
+// 256 x 256 pair tile.  The accumulator is not double-buffered: the epilogue drains it in two
+// halves and frees each as soon as it is read (tempty[0], tempty[1]); the MMA
+// issuer starts the next tile's half-0 MMAs once half 0 is free and holds the
+// half-1 MMAs of the first stages until half 1 is free (a stage is released
+// only after both halves read it).
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_out = smem + kStagesW * kStageWBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kStageOut2Bytes);
+  uint64_t* empty = full + kStagesW;
+  uint64_t* tfull = empty + kStagesW;  // [1]
+  uint64_t* tempty = tfull + 1;        // [2] one per 256-column half (used in the even CTA)
+  uint64_t* drain = tempty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* sched_full = reinterpret_cast<uint64_t*>(const_cast<int*>(abort_flag) + 1);  // [kSched]
+  uint64_t* sched_empty = sched_full + kSched;  // [kSched] (used in the even CTA)
+  volatile int32_t* sched_item = reinterpret_cast<volatile int32_t*>(sched_empty + kSched);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t crank = cluster_rank();
+  const bool leader = crank == 0;
+  constexpr bool B_MN = MODE == DX_MAIN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesW; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    for (int h = 0; h < 2; ++h) mbar_init(&tempty[h], 8);  // one arrival per epilogue warp of both CTAs
+    mbar_init(drain, 1);
+    for (int q = 0; q < kSched; ++q) {
+      mbar_init(&sched_full[q], 1);
+      mbar_init(&sched_empty[q], 2 * (1 + 4));
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    bool dep_done = !p.pdl_wait;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0, issued_par = 0;
+    bool ok = true;
+    const uint64_t pol_keep = policy_evict_last(), pol_norm = policy_evict_normal();
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    const uint32_t peer_item0 = mapa(su32(const_cast<int32_t*>(sched_item)), 1);
+    const uint32_t peer_full0 = mapa(su32(sched_full), 1), even_empty0 = mapa(su32(sched_empty), 0);
+    int claimed = -2;
+    for (int item = 0; ok;) {
+      if (leader) {
+        if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+        const int i = claimed == -2 ? atomicAdd(p.counter, 1) : claimed;
+        claimed = -2;
+        item = i < p.n_items ? i : -1;
+        sq.item[sq.q] = item;
+        st_cluster_s32(peer_item0 + 4u * uint32_t(sq.q), item);
+        mbar_arrive(&sq.full[sq.q]);
+        mbar_arrive_cluster(peer_full0 + 8u * uint32_t(sq.q));
+      } else {
+        if (!sched_take(sq, true, abort_flag, p.plan.err, item)) { ok = false; break; }
+        mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      }
+      sq.advance();
+      if (item < 0) break;
+      const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
+      const int row0 = it.t * kTileRows + int(crank) * kHalfRows;
+      const int nh0 = it.nb * 512 + int(crank) * 128;  // this CTA's columns of N half 0 (half 1: + 256)
+      const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+        uint8_t* sA = smem + stage * kStageWBytes;
+        uint8_t* sB = sA + kA2Bytes;
+        const uint32_t bar = mapa(su32(&full[stage]), 0);
+        if (kb >= it.nk1 && !dep_done) {
+          grid_dep_wait();
+          dep_done = true;
+        }
+        if (leader) mbar_expect_tx(&full[stage], 2 * kStageWBytes);
+        const CUtensorMap* ma = kb < it.nk1 ? &p.mA0 : &p.mA1;
+        const CUtensorMap* mb = kb < it.nk1 ? &p.mB0 : &p.mB1;
+        int ax, ay, kk;  // A box coordinates; kk: K coordinate of the B boxes
+        if (kb < it.nk1) {
+          ax = kb * 64; ay = row0; kk = kb * 64;
+        } else {
+          const int c = it.c0 + kb - it.nk1;
+          ax = 0; ay = c * kTileRows + int(crank) * kHalfRows; kk = p.plan.chunks[c].pcol;
+        }
+        tma_load_pair(sA, ma, bar, ax, ay, pol_norm);
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* dst = sB + h * kBHalfBytes;
+          const int n = nh0 + h * 256;  // past the end of N the boxes fill zeros (still counted)
+          if (!B_MN) {
+            tma_load_pair(dst, mb, bar, kk, n, pol_keep);
+          } else {
+            for (int i = 0; i < 2; ++i) tma_load_pair(dst + i * kBox64, mb, bar, n + 64 * i, kk, pol_keep);
+          }
+        }
+        issued |= 1u << stage;
+        issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStagesW) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!dep_done) grid_dep_wait();
+    if (!ok && leader) {
+      const unsigned long long t0 = now_ns();
+      for (int s = 0; s < kStagesW; ++s) {
+        if (!((issued >> s) & 1u)) continue;
+        while (!mbar_try(su32(&full[s]), (issued_par >> s) & 1u)) {
+          if (now_ns() - t0 > kTimeoutNs) break;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t acc_phase = 0;  // flips once per item (the single accumulator)
+    bool ok = true;
+    const uint32_t b_lbo = B_MN ? uint32_t(kBox64) : 16u;
+    const uint32_t a_step = 32 >> 4;
+    const uint32_t b_step = B_MN ? (16 * 128) >> 4 : 32 >> 4;
+    const uint32_t idesc = idesc_16(256, 256, false, B_MN, p.f16 != 0);
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    // np consecutive stages from (pend_stage, pend_kb) whose half-1 MMAs wait
+    // for half 1 of the accumulator to be drained
+    int pend_stage = 0, pend_kb = 0;
+    for (int item = 0; ok;) {
+      if (!sched_take(sq, false, abort_flag, p.plan.err, item)) { ok = false; break; }
+      mbar_arrive(&sq.empty[sq.q]);
+      sq.advance();
+      if (item < 0) break;
+      const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
+      if (!mbar_wait(&tempty[0], acc_phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+      tc_fence_after();
+      bool half1 = false;  // half 1 of the accumulator is free for this item
+      int np = 0;
+      auto mma_half = [&](int h, int st, int kb) {
+        const uint32_t sA = su32(smem + st * kStageWBytes);
+        const uint64_t ad = sdesc(sA, 16u, 1024);
+        const uint64_t bd = sdesc(sA + kA2Bytes + uint32_t(h) * kBHalfBytes, b_lbo, 1024);
+        const uint32_t d = tmem + uint32_t(h * kAccCols);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_pair(d, ad + uint64_t(k * a_step), bd + uint64_t(k * b_step), idesc, (kb | k) != 0);
+      };
+      auto flush = [&]() {  // the held half-1 MMAs, then release their stages
+        for (int i = 0, st = pend_stage; i < np; ++i, st = st + 1 == kStagesW ? 0 : st + 1) {
+          mma_half(1, st, pend_kb + i);
+          tc_commit_pair_both(&empty[st]);
+        }
+        np = 0;
+      };
+      for (int kb = 0; kb < it.nk; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.plan.err)) { ok = false; break; }
+        tc_fence_after();
+        mma_half(0, stage, kb);
+        if (!half1) half1 = mbar_try(su32(&tempty[1]), acc_phase ^ 1);
+        if (!half1 && np == kStagesW - 1) {
+          // every other stage already holds half-0-only work: wait for half 1
+          if (!mbar_wait(&tempty[1], acc_phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+          half1 = true;
+        }
+        if (half1) {
+          tc_fence_after();
+          flush();
+          mma_half(1, stage, kb);
+          tc_commit_pair_both(&empty[stage]);
+        } else {
+          if (np++ == 0) {
+            pend_stage = stage;
+            pend_kb = kb;
+          }
+        }
+        if (++stage == kStagesW) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (np > 0) {  // a short item: its held half-1 MMAs
+        if (!mbar_wait(&tempty[1], acc_phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+        tc_fence_after();
+        flush();
+      }
+      tc_commit_pair_both(tfull);
+      acc_phase ^= 1;
+    }
+    tc_commit_pair_local(drain);
+    const unsigned long long t0 = now_ns();
+    while (!mbar_try(su32(drain), 0)) {
+      if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
+    }
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quad = warp % 4;
+    const uint32_t tempty_even0 = mapa(su32(&tempty[0]), 0), tempty_even1 = mapa(su32(&tempty[1]), 0);
+    const uint32_t obuf = su32(stage_out) + uint32_t(warp - 2) * 4096u;
+    uint32_t slices = 0;
+    uint32_t acc_phase = 0;
+    SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
+    const uint32_t even_empty0 = mapa(su32(sched_empty), 0);
+    for (int item = 0;;) {
+      if (!sched_take(sq, !leader, abort_flag, p.plan.err, item)) break;
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&sq.empty[sq.q]);
+        else mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      }
+      sq.advance();
+      if (item < 0) break;
+      const Item it = decode<MODE>(p, item, 1);
+      if (it.skip) continue;
+      if (!mbar_wait(tfull, acc_phase, abort_flag, p.plan.err)) break;
+      tc_fence_after();
+      const int N = MODE == FWD_MAIN ? p.d_out : p.d_in;
+      const int64_t row_w0 = int64_t(it.t) * kTileRows + int(crank) * kHalfRows + quad * 32;
+      const bool empty_acc = it.nk == 0;
+      for (int h = 0; h < 2; ++h) {
+        const int n0 = it.nb * 512 + h * 256;
+        const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + uint32_t(h * kAccCols);
+        for (int col = 0; col < kAccCols; col += 32) {
+          if (n0 + col >= N) break;
+          epi_main_slice<MODE, 2>(p, row_w0, n0, col, empty_acc, tbase + col, obuf + (slices & 1u) * 2048u, lane);
+          ++slices;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(h ? tempty_even1 : tempty_even0);  // this half is free
+        if (MODE == FWD_MAIN && p.ar_on && n0 < N) ar_arrive(p, it.t, lane);
+      }
+      acc_phase ^= 1;
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1359,14 +1636,32 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
 }
 
-// Raster of a main launch with n_m 256-row tiles x n_n 256-wide N blocks and
-// K-extent k (bf16; A tiles and B blocks are both 256 x k).  Measured on B200
+template <int MODE>
+int launch2w(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
+  if (prm.n_items <= 0) return MLORA_OK;
+  const int sms = cta_budget(max_ctas);
+  if (sms < 2) return MLORA_ERR_UNSUPPORTED;
+  MLORA_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(&k_tc2w<MODE>), kSmemW));
+  prm.counter = prm.plan.counters + MODE;  // zeroed by the plan upload of this API call
+  const int pairs = std::min(prm.n_items, sms / 2);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  const bool timed = timing_begin(st, ev);
+  if (timed || !pdl_enabled()) pdl = false;
+  prm.pdl_wait = pdl ? 1 : 0;
+  MLORA_CUDA_TRY(launch_k(k_tc2w<MODE>, dim3(2 * pairs), kSmemW, st, pdl, prm));
+  count_launch();
+  if (timed) timing_end(MODE, st, ev);
+  return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
+}
+
+// Raster of a main launch with n_m 256-row tiles x n_n N blocks of `width`
+// columns and K-extent k (16-bit; an A tile is 256 x k, a B block width x k).  Measured on B200
 // (c2 shapes, a sweep of orientations and group sizes on one box): the 1-SM
 // mainloop is fastest with groups of M tiles sweeping N, the 2-SM mainloop
 // with groups of N blocks sweeping M, both with about 48 MB of the
 // group's stationary operand (4..16 tiles or blocks).
-void choose_raster(TcParams& prm, bool pair, int n_m, int n_n, int k) {
-  const double tile = 256.0 * k * 2.0;
+void choose_raster(TcParams& prm, bool pair, int n_m, int n_n, int k, int width = 256) {
+  const double tile = (pair ? double(width) : 256.0) * k * 2.0;
   const int g = std::max(4, std::min(16, int(48.0 * (1 << 20) / tile + 0.5)));
   prm.raster_n = pair ? 1 : 0;
   prm.group = std::max(1, std::min(g, pair ? n_n : n_m));
@@ -1448,7 +1743,10 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
   prm.tile0 = a.t0;
   prm.n_tiles_rng = a.t1 - a.t0;
   prm.n_nblk = (a.d_out + 255) / 256;
-  if (!raster_override("MLORA_RASTER_FWD", prm)) choose_raster(prm, a.pair_fwd, prm.n_tiles_rng, prm.n_nblk, a.d_in);
+  const bool wide = a.pair_fwd && a.wide;
+  prm.n_rblk = wide ? (a.d_out + 511) / 512 : prm.n_nblk;
+  if (!raster_override("MLORA_RASTER_FWD", prm))
+    choose_raster(prm, a.pair_fwd, prm.n_tiles_rng, prm.n_rblk, a.d_in, wide ? 512 : 256);
   prm.nk_main = a.W ? (a.d_in + 63) / 64 : 0;  // W == nullptr: LoRA delta only
   prm.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   prm.out = reinterpret_cast<__nv_bfloat16*>(a.Y);
@@ -1468,8 +1766,9 @@ int tc_forward(const TcCall& a, cudaStream_t st) {
     return MLORA_ERR_UNSUPPORTED;
   }
   if (a.pair_fwd) {
-    prm.n_items = prm.n_tiles_rng * prm.n_nblk;
-    return launch2<FWD_MAIN>(prm, st, a.max_ctas, after_shrink);
+    prm.n_items = prm.n_tiles_rng * prm.n_rblk;
+    return wide ? launch2w<FWD_MAIN>(prm, st, a.max_ctas, after_shrink)
+                : launch2<FWD_MAIN>(prm, st, a.max_ctas, after_shrink);
   }
   prm.n_items = 2 * prm.n_tiles_rng * prm.n_nblk;
   set_ring(prm, kA1Bytes, 4 * kBox64);
@@ -1506,14 +1805,18 @@ int tc_backward(const TcCall& a, cudaStream_t st) {
     prm.tile0 = 0;
     prm.n_tiles_rng = a.plan.n_tiles;
     prm.n_nblk = (a.d_in + 255) / 256;
-    if (!raster_override("MLORA_RASTER_DX", prm)) choose_raster(prm, a.pair_dx, prm.n_tiles_rng, prm.n_nblk, a.d_out);
+    const bool wide = a.pair_dx && a.wide;
+    prm.n_rblk = wide ? (a.d_in + 511) / 512 : prm.n_nblk;
+    if (!raster_override("MLORA_RASTER_DX", prm))
+      choose_raster(prm, a.pair_dx, prm.n_tiles_rng, prm.n_rblk, a.d_out, wide ? 512 : 256);
     prm.nk_main = a.W ? (a.d_out + 63) / 64 : 0;
     prm.out = reinterpret_cast<__nv_bfloat16*>(a.dX);
     prm.out_rows = a.out_rows;
     if (!make_out_map(&prm.mY, a.dX, a.M, a.d_in)) return MLORA_ERR_UNSUPPORTED;
     if (a.pair_dx) {
-      prm.n_items = a.plan.n_tiles * prm.n_nblk;
-      s = launch2<DX_MAIN>(prm, st, a.max_ctas, after_shrink);
+      prm.n_items = a.plan.n_tiles * prm.n_rblk;
+      s = wide ? launch2w<DX_MAIN>(prm, st, a.max_ctas, after_shrink)
+               : launch2<DX_MAIN>(prm, st, a.max_ctas, after_shrink);
     } else {
       prm.n_items = 2 * a.plan.n_tiles * prm.n_nblk;
       set_ring(prm, kA1Bytes, 4 * kBox64);

@@ -29,6 +29,7 @@ struct TcCall {
   float lr = 0.f;  // fused SGD step (MLORA_BWD_SGD_A / _B in bwd_stages)
   bool pair_fwd = false;  // forward mainloop on 2-SM pairs (tcgen05 cta_group::2)
   bool pair_dx = true;    // dX mainloop on 2-SM pairs
+  bool wide = false;      // the pair mainloops on 256 x 512 tiles (k_tc2w) instead of 256 x 256
   // forward MAIN: push the partial tiles to their owner ranks (mlora_forward_push)
   const mlora_peer_ar* ar = nullptr;
 };

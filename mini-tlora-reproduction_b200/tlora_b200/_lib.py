@@ -50,6 +50,7 @@ IMPL_SIMT = 1
 IMPL_TC = 2
 IMPL_TC_1SM = 3
 IMPL_TC_2SM = 4
+IMPL_TC_WIDE = 5
 
 _c_int32_p = ctypes.POINTER(ctypes.c_int32)
 _c_float_p = ctypes.POINTER(ctypes.c_float)

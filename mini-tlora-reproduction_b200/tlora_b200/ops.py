@@ -22,7 +22,7 @@ from ._lib import BF16, F16, F32, RANK_CHUNK, TILE_ROWS
 
 _DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 _IMPLS = {"auto": _lib.IMPL_AUTO, "simt": _lib.IMPL_SIMT, "tc": _lib.IMPL_TC, "tc1": _lib.IMPL_TC_1SM,
-          "tc2": _lib.IMPL_TC_2SM}
+          "tc2": _lib.IMPL_TC_2SM, "tcw": _lib.IMPL_TC_WIDE}
 
 
 def mlora_dtype(dt: torch.dtype) -> int:

@@ -141,7 +141,7 @@ def test_config0_fp32_full_size():
 
 
 @pytest.mark.parametrize("cfg,scale", [("c1", 0.125), ("c2", 0.0625), ("c3", 0.0625), ("c4", 0.03125)])
-@pytest.mark.parametrize("impl", ["tc", "tc1", "tc2", "simt"])
+@pytest.mark.parametrize("impl", ["tc", "tc1", "tc2", "tcw", "simt"])
 def test_bf16_configs_scaled(cfg, scale, impl):
     """bf16 configurations at reduced size: native kernels vs the fp64 oracle
     on the same bf16-rounded inputs."""
@@ -153,7 +153,7 @@ def test_bf16_configs_scaled(cfg, scale, impl):
 
 
 @pytest.mark.parametrize("cfg,scale", [("c2", 0.0625), ("c4", 0.03125)])
-@pytest.mark.parametrize("impl", ["tc", "tc2", "simt"])
+@pytest.mark.parametrize("impl", ["tc", "tc2", "tcw", "simt"])
 def test_fp16_configs_scaled(cfg, scale, impl):
     """fp16, the element type of the reference's GPU kernels
     (phase5c_fused_triton.py, phase5d_triton_training.py): forward, backward
@@ -209,7 +209,8 @@ EDGE_CASES = {
 
 
 @pytest.mark.parametrize("dtype,impl", [(torch.float32, "simt"), (torch.bfloat16, "tc1"), (torch.bfloat16, "tc2"),
-                                        (torch.float16, "tc1"), (torch.float16, "tc2"), (torch.float16, "simt")])
+                                        (torch.bfloat16, "tcw"), (torch.float16, "tc1"), (torch.float16, "tc2"),
+                                        (torch.float16, "tcw"), (torch.float16, "simt")])
 @pytest.mark.parametrize("case", sorted(EDGE_CASES))
 def test_edge_cases(case, dtype, impl):
     d_in, d_out, ranks, idf = EDGE_CASES[case]
@@ -239,16 +240,17 @@ def test_delta_only(dtype, impl):
 
 
 def test_tc_matches_simt_bf16():
-    """The kernel families agree on the same bf16 inputs; the 2-SM and 1-SM
-    mainloops accumulate identically (same K order), so they agree bit for bit."""
+    """The kernel families agree on the same bf16 inputs; the 1-SM, 2-SM and
+    wide 2-SM mainloops accumulate identically (same K order), so they agree
+    bit for bit."""
     w = workloads.build(workloads.spec("c1", 0.125), device=DEV)
     outs = {}
-    for impl in ("tc", "tc1", "tc2", "simt"):
+    for impl in ("tc", "tc1", "tc2", "tcw", "simt"):
         w.model.impl = impl
         outs[impl] = module_step(w.model, w.x, w.ids, w.dy)
     for u, v in zip(outs["tc"][:2], outs["simt"][:2]):
         assert orc.relative_l2(u, v) <= 1e-2
-    for other in ("tc1", "tc2"):
+    for other in ("tc1", "tc2", "tcw"):
         for u, v in zip(outs["tc"][:2], outs[other][:2]):
             assert np.array_equal(u, v)
 
@@ -306,7 +308,7 @@ def test_staged_backward_matches_backward(dtype, impl):
         assert torch.equal(bw.dB[:, o:o + r], dB[:, o:o + r])
 
 
-@pytest.mark.parametrize("impl", ["tc", "tc1", "tc2"])
+@pytest.mark.parametrize("impl", ["tc", "tc1", "tc2", "tcw"])
 @pytest.mark.parametrize("max_ctas", [2, 3, 7])
 def test_scheduler_result_independent_of_cta_count(impl, max_ctas):
     """The persistent kernels hand work items out dynamically; with only a few

@@ -76,7 +76,7 @@ def _emulated(w, world, impl, n_nano, timeout_s=2.0):
 
 
 @pytest.mark.parametrize("world,impl,n_nano", [(2, "tc", 1), (2, "tc", 3), (3, "tc", 2), (4, "tc", 4),
-                                               (2, "tc2", 2), (8, "tc", 3)])
+                                               (2, "tc2", 2), (2, "tcw", 2), (3, "tcw", 1), (8, "tc", 3)])
 def test_push_allreduce_c3_scaled(world, impl, n_nano):
     """c3 (32 jobs, ranks 8-64) at 1/8 of its features and rows: 1024 x 1024,
     about 5k rows."""

@@ -72,7 +72,7 @@ def test_misaligned_pointers_rejected_before_any_launch():
         return lib.mlora_forward(ctypes.byref(args.prob), ctypes.byref(args.route), x, P[1], bias, P[2], P[3],
                                  P[4], P[5], P[6], wb, None)
 
-    for impl in ("tc", "tc1", "tc2"):
+    for impl in ("tc", "tc1", "tc2", "tcw"):
         assert fwd(impl, ctypes.c_void_p(base + 2)) == _lib.ERR_UNSUPPORTED  # bias 2 bytes in
         assert fwd(impl, P[7], x=ctypes.c_void_p(base + 8)) == _lib.ERR_UNSUPPORTED
     for impl in ("tc", "simt", "auto"):  # odd address: not even element-aligned
