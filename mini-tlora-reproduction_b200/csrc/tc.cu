@@ -386,11 +386,12 @@ __device__ __forceinline__ float ld1(const __nv_bfloat16* src, bool f16) {
   const unsigned short b = *reinterpret_cast<const unsigned short*>(src);
   return f16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
 }
-// P <- P - lr G for one element, G = v as stored in 16 bits (the fused SGD
-// step; the same expression as the separate SGD pass)
-__device__ __forceinline__ void sgd1(__nv_bfloat16* P, float v, float lr, bool f16) {
+// P - lr G for one element of weight P (as loaded) and gradient G = v as
+// stored in 16 bits (the fused SGD step; the same expression as the separate
+// SGD pass)
+__device__ __forceinline__ float sgd_new(float P, float v, float lr, bool f16) {
   const float g = f16 ? __half2float(__float2half_rn(v)) : __bfloat162float(__float2bfloat16_rn(v));
-  st1(P, ld1(P, f16) - lr * g, f16);
+  return P - lr * g;
 }
 __device__ __forceinline__ void store32(__nv_bfloat16* dst, const float (&f)[32], bool f16) {
   uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -949,31 +950,93 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
             if (ri.kind == 1) {
               if (d >= p.d_out) continue;
               __nv_bfloat16* dst = p.dB + int64_t(d) * p.R + pcol + col;
-              if (col + 32 <= rvalid) {
-                float f[32];
+              // this lane's 32 values are 64 contiguous bytes of row d of dB
+              // (and of B_pack): 16-byte accesses, one per 8 values.  With the
+              // fused SGD the old weights are loaded first, as whole 16-byte
+              // groups; elements past the rank keep their bits.
+              uint4* P4 = p.B_upd ? reinterpret_cast<uint4*>(p.B_upd + int64_t(d) * p.R + pcol + col) : nullptr;
+              uint4 old4[4];
+              if (P4) {
 #pragma unroll
-                for (int q = 0; q < 32; ++q) f[q] = __uint_as_float(v[q]);
-                store32(dst, f, p.f16);
-              } else {
-#pragma unroll
-                for (int q = 0; q < 32; ++q)
-                  if (col + q < rvalid) st1(dst + q, __uint_as_float(v[q]), p.f16);
+                for (int c = 0; c < 4; ++c)
+                  if (col + 8 * c < rvalid) old4[c] = P4[c];
               }
-              if (p.B_upd) {  // fused SGD step on the same elements of B_pack
-                __nv_bfloat16* P = p.B_upd + int64_t(d) * p.R + pcol + col;
 #pragma unroll
-                for (int q = 0; q < 32; ++q)
-                  if (col + q < rvalid) sgd1(P + q, __uint_as_float(v[q]), p.lr, p.f16);
+              for (int c = 0; c < 4; ++c) {
+                const int c0 = col + 8 * c;  // rank column of the group's first element
+                if (c0 >= rvalid) break;
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[8 * c + e]);
+                if (c0 + 8 <= rvalid) {
+                  reinterpret_cast<uint4*>(dst)[c] = make_uint4(pack2(f[0], f[1], p.f16), pack2(f[2], f[3], p.f16),
+                                                                pack2(f[4], f[5], p.f16), pack2(f[6], f[7], p.f16));
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    if (c0 + e < rvalid) st1(dst + 8 * c + e, f[e], p.f16);
+                }
+                if (P4) {  // fused SGD step on the same elements of B_pack
+                  uint32_t w[4] = {old4[c].x, old4[c].y, old4[c].z, old4[c].w};
+#pragma unroll
+                  for (int h = 0; h < 4; ++h) {
+                    const float2 o = unpack2(w[h], p.f16);
+                    const uint32_t nw = pack2(sgd_new(o.x, f[2 * h], p.lr, p.f16),
+                                              sgd_new(o.y, f[2 * h + 1], p.lr, p.f16), p.f16);
+                    const uint32_t keep = (c0 + 2 * h < rvalid ? 0u : 0xffffu) |
+                                          (c0 + 2 * h + 1 < rvalid ? 0u : 0xffff0000u);
+                    w[h] = (nw & ~keep) | (w[h] & keep);
+                  }
+                  P4[c] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
               }
             } else {
-              if (d >= p.d_in) continue;
+              // dA is [rank row, d_in]: the warp's 32 rows d0.. of the d block
+              // x 32 rank columns go through the warp's staging buffer
+              // (transposed, XOR-swizzled 16-byte groups, conflict-free both
+              // ways) so that lane q then owns rank row col + q: 64
+              // contiguous bytes of dA (and of A_pack for the fused SGD step)
+              // as four 16-byte accesses.  d_in is a multiple of 8, so each
+              // 8-element group is wholly inside d_in or wholly outside.
+              uint8_t* tb = stage_out + (warp - 2) * 2048;
+              const int d0 = ri.block * 128 + quad * 32;
+              __syncwarp();  // the previous slice's reads of the buffer are done
 #pragma unroll
-              for (int q = 0; q < 32; ++q)
-                if (col + q < rvalid) {
-                  const int64_t e = int64_t(pcol + col + q) * p.d_in + d;
-                  st1(p.dA + e, __uint_as_float(v[q]), p.f16);
-                  if (p.A_upd) sgd1(p.A_upd + e, __uint_as_float(v[q]), p.lr, p.f16);  // fused SGD step
+              for (int q = 0; q < 32; ++q) {
+                const float g = __uint_as_float(v[q]);
+                const uint16_t b =
+                    p.f16 ? __half_as_ushort(__float2half_rn(g)) : __bfloat16_as_ushort(__float2bfloat16_rn(g));
+                *reinterpret_cast<uint16_t*>(tb + q * 64 + ((((lane >> 3) ^ (q >> 1)) & 3) << 4) + (lane & 7) * 2) = b;
+              }
+              __syncwarp();
+              if (col + lane < rvalid) {
+                const int q = lane;
+                const int64_t e0 = int64_t(pcol + col + q) * p.d_in + d0;
+                uint4 gv[4], old[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                  gv[c] = *reinterpret_cast<const uint4*>(tb + q * 64 + (((c ^ (q >> 1)) & 3) << 4));
+                if (p.A_upd) {
+#pragma unroll
+                  for (int c = 0; c < 4; ++c)
+                    if (d0 + 8 * c < p.d_in) old[c] = reinterpret_cast<const uint4*>(p.A_upd + e0)[c];
                 }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  if (d0 + 8 * c >= p.d_in) break;
+                  reinterpret_cast<uint4*>(p.dA + e0)[c] = gv[c];
+                  if (p.A_upd) {  // fused SGD step on the same elements of A_pack
+                    const uint32_t gw[4] = {gv[c].x, gv[c].y, gv[c].z, gv[c].w};
+                    uint32_t ow[4] = {old[c].x, old[c].y, old[c].z, old[c].w};
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                      const float2 g2 = unpack2(gw[h], p.f16), o2 = unpack2(ow[h], p.f16);
+                      ow[h] = pack2(sgd_new(o2.x, g2.x, p.lr, p.f16), sgd_new(o2.y, g2.y, p.lr, p.f16), p.f16);
+                    }
+                    reinterpret_cast<uint4*>(p.A_upd + e0)[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+                  }
+                }
+              }
             }
           }
         }
