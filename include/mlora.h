@@ -75,8 +75,9 @@ extern "C" {
 /* kernel family selection for mlora_forward / mlora_backward */
 #define MLORA_IMPL_AUTO 0   /* tcgen05 tensor-core kernels when the shape allows, else SIMT */
 #define MLORA_IMPL_SIMT 1   /* CUDA-core kernels, fp32 accumulate (exact fp32 mode) */
-#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 or fp16); forward mainloop on single
-                               SMs, dX mainloop on 2-SM pairs (the faster variant of each, measured) */
+#define MLORA_IMPL_TC 2     /* tcgen05/TMEM kernels fed by TMA (bf16 or fp16); forward mainloop on 2-SM
+                               pairs when d_in >= 2048, else on single SMs; dX mainloop on 2-SM pairs
+                               (the faster variant at each size, measured) */
 #define MLORA_IMPL_TC_1SM 3 /* as MLORA_IMPL_TC with both mainloops on single SMs (comparison path) */
 #define MLORA_IMPL_TC_2SM 4 /* as MLORA_IMPL_TC with both mainloops on 2-SM pairs (comparison path) */
 #define MLORA_IMPL_TC_WIDE 5 /* as MLORA_IMPL_TC_2SM with 256 x 512 pair tiles (comparison path) */

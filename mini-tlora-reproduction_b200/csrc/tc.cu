@@ -17,11 +17,11 @@
 // separate cuBLAS backbone (phase5c_fused_triton.py:555) and the per-adapter
 // PyTorch backward (phase5d_triton_training.py:248-325).
 //
-// Two kernel templates, both persistent and warp-specialised (192 threads:
-// warp 0 lane 0 issues TMA loads into a shared-memory ring, warp 1 owns TMEM
-// (512 columns = two 128x256 fp32 accumulators) and lane 0 issues
-// tcgen05.mma, warps 2..5 drain the previous work item's accumulator with
-// tcgen05.ld while the next one accumulates):
+// Three kernel templates, all persistent and warp-specialised (224 threads:
+// lane 0 of warps 0 and 6 issues TMA loads into a shared-memory ring, the two
+// taking alternate k-blocks; warp 1 owns TMEM (512 columns = two 128x256 fp32
+// accumulators) and lane 0 issues tcgen05.mma; warps 2..5 drain the previous
+// work item's accumulator with tcgen05.ld while the next one accumulates):
 //
 //  * k_tc2 (FWD_MAIN, DX_MAIN): a cluster of two CTAs on two SMs computes a
 //    256x256 tile with tcgen05.mma.cta_group::2 (M = 256, N = 256).  Each CTA
@@ -63,7 +63,13 @@
 namespace mlora {
 namespace {
 
-constexpr int kThreads = 192;
+// Threads per CTA: warp 0 and warp 6 issue the TMA loads (alternate
+// k-blocks), warp 1 owns TMEM and issues the MMAs, warps 2..5 drain the
+// accumulator.  One issuing warp keeps only about three TMA copies in flight
+// (measured on B200: a streaming read from HBM ran at 43-54 GB/s per SM with
+// one issuing warp whatever the ring depth, 64 GB/s with two and 118 GB/s
+// with four), which held the mainloops below the tensor pipe's rate.
+constexpr int kThreads = 224;
 constexpr int kBox64 = 64 * 64 * 2;  // one 64x64 bf16 box, 8 KB
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 256;
@@ -730,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     mbar_init(drain, 1);
     for (int q = 0; q < kSched; ++q) {
       mbar_init(&sched_full[q], 1);
-      mbar_init(&sched_empty[q], 1 + 4);  // the MMA thread and the four epilogue warps
+      mbar_init(&sched_empty[q], 1 + 4 + 1);  // the MMA thread, the four epilogue warps, the second producer
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -747,19 +753,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
   const uint32_t tmem = *tmem_slot;
 
   if (MODE == SHRINK_FWD || MODE == SHRINK_BWD) grid_dep_launch();  // the mainloop after it may start
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer
+  if ((warp == 0 || warp == 6) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers
+    // Warp 0 claims the work items and publishes them; warp 6 takes them from
+    // the queue.  Both walk every k-block; k-block g of the launch (counted
+    // across items) is loaded by warp 0 when g is even, by warp 6 when odd.
+    const uint32_t pid = warp == 0 ? 0u : 1u;
+    uint32_t gk = 0;
     bool dep_done = !p.pdl_wait;  // the shrink before this launch is known complete
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
+    uint32_t issued = 0, issued_par = 0;  // per stage: this warp issued a load / its phase parity
     bool ok = true;
     const uint64_t pol_keep = policy_evict_last(), pol_stream = policy_evict_first(),
                    pol_norm = policy_evict_normal();
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
     int claimed = -2;
     for (int item = 0; ok;) {
-      if (!sched_next(sq, p.counter, p.n_items, abort_flag, p.plan.err, claimed, item)) { ok = false; break; }
+      if (pid == 0) {
+        if (!sched_next(sq, p.counter, p.n_items, abort_flag, p.plan.err, claimed, item)) { ok = false; break; }
+      } else {
+        if (!sched_take(sq, false, abort_flag, p.plan.err, item)) { ok = false; break; }
+        mbar_arrive(&sq.empty[sq.q]);
+        sq.advance();
+      }
       if (item < 0) break;
       const Item it = decode<MODE>(p, item, kUnits);
       if (it.skip) continue;
@@ -778,63 +795,65 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
       }
 
       for (int kb = 0; kb < it.nk; ++kb) {
-        if (kb == claim_kb) claimed = atomicAdd(p.counter, 1);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
-        uint8_t* sA = smem + stage * stage_bytes;
-        uint8_t* sB = sA + kA1Bytes;
-        uint64_t* bar = &full[stage];
-        if ((MODE == FWD_MAIN || MODE == DX_MAIN) && kb >= it.nk1 && !dep_done) {
-          grid_dep_wait();  // the intermediate is the shrink's output
-          dep_done = true;
+        if (pid == 0 && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if ((gk++ & 1u) == pid) {  // this warp's k-block
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
+          uint8_t* sA = smem + stage * stage_bytes;
+          uint8_t* sB = sA + kA1Bytes;
+          uint64_t* bar = &full[stage];
+          if ((MODE == FWD_MAIN || MODE == DX_MAIN) && kb >= it.nk1 && !dep_done) {
+            grid_dep_wait();  // the intermediate is the shrink's output
+            dep_done = true;
+          }
+          if (MODE == FWD_MAIN) {
+            mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
+            if (kb < it.nk1) {
+              tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
+              tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256, pol_keep);
+            } else {
+              const int c = it.c0 + kb - it.nk1;
+              tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
+              tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256, pol_keep);
+            }
+          } else if (MODE == DX_MAIN) {
+            mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
+            if (kb < it.nk1) {
+              tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
+              for (int i = 0; i < 4; ++i)
+                tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64, pol_keep);
+            } else {
+              const int c = it.c0 + kb - it.nk1;
+              const int pcol = p.plan.chunks[c].pcol;
+              tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
+              for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol, pol_keep);
+            }
+          } else if (MODE == SHRINK_FWD) {
+            mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
+            for (int i = 0; i < it.nc; ++i)
+              tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol, pol_keep);
+          } else if (MODE == SHRINK_BWD) {
+            mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
+            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
+            for (int i = 0; i < it.nc; ++i)
+              tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64, pol_keep);
+          } else {  // REDUCE: k-block kb = slice r_q of list entry r_e
+            const CUtensorMap* ma = it.ri.kind == 0 ? &p.mA0 : &p.mA1;
+            const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
+            mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
+            for (int i = 0; i < 2; ++i)
+              tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, r_d.y * kTileRows + 64 * r_q, pol_stream);
+            for (int i = 0; i < it.nc; ++i)
+              tma_load(sB + i * kBox64, mb, bar, 0, (r_d.x + it.ri.j0 + i) * kTileRows + 64 * r_q, pol_norm);
+          }
+          issued |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
         }
-        if (MODE == FWD_MAIN) {
-          mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
-          if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
-            tma_load(sB, &p.mB0, bar, kb * 64, it.nb * 256, pol_keep);
-          } else {
-            const int c = it.c0 + kb - it.nk1;
-            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
-            tma_load(sB, &p.mB1, bar, p.plan.chunks[c].pcol, it.nb * 256, pol_keep);
-          }
-        } else if (MODE == DX_MAIN) {
-          mbar_expect_tx(bar, kA1Bytes + 4 * kBox64);
-          if (kb < it.nk1) {
-            tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_norm);
-            for (int i = 0; i < 4; ++i)
-              tma_load(sB + i * kBox64, &p.mB0, bar, it.nb * 256 + 64 * i, kb * 64, pol_keep);
-          } else {
-            const int c = it.c0 + kb - it.nk1;
-            const int pcol = p.plan.chunks[c].pcol;
-            tma_load(sA, &p.mA1, bar, 0, c * kTileRows + it.half * kHalfRows, pol_norm);
-            for (int i = 0; i < 4; ++i) tma_load(sB + i * kBox64, &p.mB1, bar, it.nb * 256 + 64 * i, pcol, pol_keep);
-          }
-        } else if (MODE == SHRINK_FWD) {
-          mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
-          for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, &p.mB0, bar, kb * 64, p.plan.chunks[it.c0 + i].pcol, pol_keep);
-        } else if (MODE == SHRINK_BWD) {
-          mbar_expect_tx(bar, kA1Bytes + it.nc * kBox64);
-          tma_load(sA, &p.mA0, bar, kb * 64, row0, pol_stream);
-          for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, &p.mB0, bar, p.plan.chunks[it.c0 + i].pcol, kb * 64, pol_keep);
-        } else {  // REDUCE: k-block kb = slice r_q of list entry r_e
-          const CUtensorMap* ma = it.ri.kind == 0 ? &p.mA0 : &p.mA1;
-          const CUtensorMap* mb = it.ri.kind == 0 ? &p.mB0 : &p.mB1;
-          mbar_expect_tx(bar, 2 * kBox64 + it.nc * kBox64);
-          for (int i = 0; i < 2; ++i)
-            tma_load(sA + i * kBox64, ma, bar, it.ri.block * 128 + 64 * i, r_d.y * kTileRows + 64 * r_q, pol_stream);
-          for (int i = 0; i < it.nc; ++i)
-            tma_load(sB + i * kBox64, mb, bar, 0, (r_d.x + it.ri.j0 + i) * kTileRows + 64 * r_q, pol_norm);
-          if (++r_q >= r_d.w && ++r_e < it.ri.le) {
-            r_d = r_n;
-            r_q = r_d.z;
-            if (r_e + 1 < it.ri.le) r_n = reduce_entry(p, r_e + 1);
-          }
+        if (MODE == REDUCE && ++r_q >= r_d.w && ++r_e < it.ri.le) {  // both warps walk the list
+          r_d = r_n;
+          r_q = r_d.z;
+          if (r_e + 1 < it.ri.le) r_n = reduce_entry(p, r_e + 1);
         }
-        issued |= 1u << stage;
-        issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
         if (++stage == n_stages) { stage = 0; phase ^= 1; }
       }
     }
@@ -894,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc(const __grid_constant__ TcPa
     while (!mbar_try(su32(drain), 0)) {
       if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
     const int r = quad * 32 + lane;  // accumulator row = TMEM lane
@@ -1098,8 +1117,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     mbar_init(drain, 1);
     for (int q = 0; q < kSched; ++q) {
       mbar_init(&sched_full[q], 1);
-      // even CTA: its MMA thread and epilogue warps, the odd CTA's producer and epilogue warps
-      mbar_init(&sched_empty[q], 2 * (1 + 4));
+      // even CTA: its MMA thread, epilogue warps and second producer; the odd
+      // CTA: its two producers and epilogue warps
+      mbar_init(&sched_empty[q], 2 * (1 + 4 + 1));
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1115,12 +1135,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer (both CTAs)
+  if ((warp == 0 || warp == 6) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers (both CTAs)
+    // Warp 0 of the even CTA claims and publishes the work items; the other
+    // producer warps take them from the queue.  k-block g of the launch
+    // (counted across items) is loaded by warp 0 of each CTA when g is even,
+    // by warp 6 when odd.
+    const uint32_t pid = warp == 0 ? 0u : 1u;
+    uint32_t gk = 0;
     bool dep_done = !p.pdl_wait;  // the shrink before this launch is known complete
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t issued = 0, issued_par = 0;  // per stage: a load was issued / its phase parity
+    uint32_t issued = 0, issued_par = 0;  // per stage: this warp issued a load / its phase parity
     bool ok = true;
     const uint64_t pol_keep = policy_evict_last(), pol_norm = policy_evict_normal();
     SchedQ sq{sched_item, sched_full, sched_empty, 0, 0};
@@ -1128,7 +1154,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     const uint32_t peer_full0 = mapa(su32(sched_full), 1), even_empty0 = mapa(su32(sched_empty), 0);
     int claimed = -2;
     for (int item = 0; ok;) {
-      if (leader) {
+      if (pid == 1) {
+        if (!sched_take(sq, !leader, abort_flag, p.plan.err, item)) { ok = false; break; }
+        if (leader) mbar_arrive(&sq.empty[sq.q]);
+        else mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      } else if (leader) {
         // publish the claimed item (claim one now if none) to both CTAs
         if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         const int i = claimed == -2 ? atomicAdd(p.counter, 1) : claimed;
@@ -1150,7 +1180,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
       const int nh = it.nb * 256 + int(crank) * 128;               // this CTA's half of the N block
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
       for (int kb = 0; kb < it.nk; ++kb) {
-        if (leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if (pid == 0 && leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if ((gk++ & 1u) != pid) {  // the other producer's k-block
+          if (++stage == kStages2) { stage = 0; phase ^= 1; }
+          continue;
+        }
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         uint8_t* sA = smem + stage * kStage2Bytes;
         uint8_t* sB = sA + kA2Bytes;
@@ -1236,7 +1270,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2(c
     while (!mbar_try(su32(drain), 0)) {
       if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quad = warp % 4;
     const uint32_t tempty_even0 = mapa(su32(&tempty[0]), 0), tempty_even1 = mapa(su32(&tempty[1]), 0);
@@ -1331,7 +1365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(
     mbar_init(drain, 1);
     for (int q = 0; q < kSched; ++q) {
       mbar_init(&sched_full[q], 1);
-      mbar_init(&sched_empty[q], 2 * (1 + 4));
+      mbar_init(&sched_empty[q], 2 * (1 + 4 + 1));
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1347,8 +1381,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA producer (both CTAs)
+  if ((warp == 0 || warp == 6) && lane == 0) {
+    // ---------------------------------------------------------------- TMA producers (both CTAs)
+    // as in k_tc2: warp 0 loads the even k-blocks of the launch, warp 6 the odd
+    const uint32_t pid = warp == 0 ? 0u : 1u;
+    uint32_t gk = 0;
     bool dep_done = !p.pdl_wait;
     int stage = 0;
     uint32_t phase = 0;
@@ -1360,7 +1397,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(
     const uint32_t peer_full0 = mapa(su32(sched_full), 1), even_empty0 = mapa(su32(sched_empty), 0);
     int claimed = -2;
     for (int item = 0; ok;) {
-      if (leader) {
+      if (pid == 1) {
+        if (!sched_take(sq, !leader, abort_flag, p.plan.err, item)) { ok = false; break; }
+        if (leader) mbar_arrive(&sq.empty[sq.q]);
+        else mbar_arrive_cluster(even_empty0 + 8u * uint32_t(sq.q));
+      } else if (leader) {
         if (!mbar_wait(&sq.empty[sq.q], sq.ph ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         const int i = claimed == -2 ? atomicAdd(p.counter, 1) : claimed;
         claimed = -2;
@@ -1381,7 +1422,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(
       const int nh0 = it.nb * 512 + int(crank) * 128;  // this CTA's columns of N half 0 (half 1: + 256)
       const int claim_kb = it.nk > kClaimAhead ? it.nk - kClaimAhead : 0;
       for (int kb = 0; kb < it.nk; ++kb) {
-        if (leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if (pid == 0 && leader && kb == claim_kb) claimed = atomicAdd(p.counter, 1);
+        if ((gk++ & 1u) != pid) {  // the other producer's k-block
+          if (++stage == kStagesW) { stage = 0; phase ^= 1; }
+          continue;
+        }
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.plan.err)) { ok = false; break; }
         uint8_t* sA = smem + stage * kStageWBytes;
         uint8_t* sB = sA + kA2Bytes;
@@ -1503,7 +1548,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_tc2w(
     while (!mbar_try(su32(drain), 0)) {
       if (now_ns() - t0 > kTimeoutNs) { flag_error(p.plan.err, kErrTimeout); break; }
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quad = warp % 4;
     const uint32_t tempty_even0 = mapa(su32(&tempty[0]), 0), tempty_even1 = mapa(su32(&tempty[1]), 0);
@@ -1639,10 +1684,10 @@ bool pdl_enabled() {
 // Launch `kern` on `st`; with `pdl`, as a programmatic dependent launch of the
 // kernel before it in the stream (it may start while that one finishes).
 template <class K>
-cudaError_t launch_k(K kern, dim3 grid, int smem, cudaStream_t st, bool pdl, const TcParams& prm) {
+cudaError_t launch_k(K kern, dim3 grid, int threads, int smem, cudaStream_t st, bool pdl, const TcParams& prm) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1675,7 +1720,7 @@ int launch1(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   const bool timed = timing_begin(st, ev);
   if (timed || !pdl_enabled()) pdl = false;  // events between the launches order them anyway
   prm.pdl_wait = pdl ? 1 : 0;
-  MLORA_CUDA_TRY(launch_k(k_tc<MODE>, dim3(grid), kSmem1, st, pdl, prm));
+  MLORA_CUDA_TRY(launch_k(k_tc<MODE>, dim3(grid), kThreads, kSmem1, st, pdl, prm));
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -1693,7 +1738,7 @@ int launch2(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   const bool timed = timing_begin(st, ev);
   if (timed || !pdl_enabled()) pdl = false;  // events between the launches order them anyway
   prm.pdl_wait = pdl ? 1 : 0;
-  MLORA_CUDA_TRY(launch_k(k_tc2<MODE>, dim3(2 * pairs), kSmem2, st, pdl, prm));
+  MLORA_CUDA_TRY(launch_k(k_tc2<MODE>, dim3(2 * pairs), kThreads, kSmem2, st, pdl, prm));
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
@@ -1711,7 +1756,7 @@ int launch2w(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
   const bool timed = timing_begin(st, ev);
   if (timed || !pdl_enabled()) pdl = false;
   prm.pdl_wait = pdl ? 1 : 0;
-  MLORA_CUDA_TRY(launch_k(k_tc2w<MODE>, dim3(2 * pairs), kSmemW, st, pdl, prm));
+  MLORA_CUDA_TRY(launch_k(k_tc2w<MODE>, dim3(2 * pairs), kThreads, kSmemW, st, pdl, prm));
   count_launch();
   if (timed) timing_end(MODE, st, ev);
   return cudaGetLastError() == cudaSuccess ? MLORA_OK : MLORA_ERR_CUDA;
