@@ -231,12 +231,19 @@ class ShardedLayer:
     all-reduce wait ran out and rows of Y hold no sum."""
 
     def __init__(self, model, rank: int, world: int, compute=None, group=None, bwd_group=None,
-                 comm: str = "nccl", err_word: Optional[torch.Tensor] = None):
+                 comm: str = "nccl", err_word: Optional[torch.Tensor] = None, dz: str = "split"):
         # `bwd_group`: a second communicator for the backward's small
         # all-reduces (dZ, dB), so they do not queue behind the large Y
-        # all-reduces still in flight on `group`
+        # all-reduces still in flight on `group`.
+        # `dz`: "split" = each rank computes dZ = s dY B for its share of the
+        # tiles and the shares are summed with an all-reduce; "replicated" =
+        # every rank computes all of dZ (dY and B_pack are replicated), no
+        # all-reduce
         if comm not in COMMS:
             raise ValueError(f"comm must be one of {COMMS}, not {comm!r}")
+        if dz not in ("split", "replicated"):
+            raise ValueError(f"dz must be 'split' or 'replicated', not {dz!r}")
+        self.dz = dz
         self.rank, self.world, self.group = rank, world, group
         self.comm = comm
         self.err_word = err_word
@@ -496,12 +503,16 @@ class ShardedLayer:
                 applied = ()
             self._mark("bwd")
             return b["dx"], b["dA"], b["dB"], None, applied
-        t0, t1 = _share(b["n_tiles"], self.rank, self.world)
-        c.bwd_dz(b, t0, t1)
-        self._mark("bwd_dz")
         hdz = None
-        if b["dz"] is not None:
-            hdz = dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.bwd_group, async_op=True)
+        if self.dz == "replicated":
+            c.bwd_dz(b, 0, b["n_tiles"])
+            self._mark("bwd_dz")
+        else:
+            t0, t1 = _share(b["n_tiles"], self.rank, self.world)
+            c.bwd_dz(b, t0, t1)
+            self._mark("bwd_dz")
+            if b["dz"] is not None:
+                hdz = dist.all_reduce(b["dz"], op=dist.ReduceOp.SUM, group=self.bwd_group, async_op=True)
         b0, b1 = _share(b["n_db"], self.rank, self.world)
         c.bwd_db(b, b0, b1)  # reads Z and dY only: runs while dZ is being summed
         hdb = dist.all_reduce(b["dB"], op=dist.ReduceOp.SUM, group=self.bwd_group, async_op=True)

@@ -120,12 +120,13 @@ def _build(seed=0):
     return m, ids, x, dy
 
 
-def _worker(rank, world, port, n_nano, pipelined, q):
+def _worker(rank, world, port, n_nano, pipelined, q, dz="split"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         m, ids, x, dy = _build()
-        layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group(list(range(world))))
+        layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group(list(range(world))),
+                             dz=dz)
         plan = ops.route(ids, layer.table, torch.device("cpu"))
         x_p = layer.shard_input(x)
         y, dx_p = layer.step(x_p, plan, dy, n_nano, lr=0.01, pipelined=pipelined)
@@ -142,13 +143,17 @@ def _worker(rank, world, port, n_nano, pipelined, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n_nano,pipelined", [(2, 1, True), (2, 3, True), (2, 2, False), (3, 4, True),
-                                                    (1, 2, True)])
-def test_sharded_step_matches_unsharded(world, n_nano, pipelined):
+@pytest.mark.parametrize("world,n_nano,pipelined,dz", [(2, 1, True, "split"), (2, 3, True, "split"),
+                                                       (2, 2, False, "split"), (3, 4, True, "split"),
+                                                       (1, 2, True, "split"), (2, 3, True, "replicated"),
+                                                       (3, 2, True, "replicated")])
+def test_sharded_step_matches_unsharded(world, n_nano, pipelined, dz):
+    """Every rank's step against the fp64 oracle of the unsharded layer; dZ
+    split across the ranks and summed, or computed whole on every rank."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, pipelined, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, pipelined, q, dz)) for r in range(world)]
     for p in procs:
         p.start()
     res = q.get(timeout=120)
