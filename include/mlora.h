@@ -272,8 +272,6 @@ typedef struct mlora_mc_ar {
   uint32_t* flags;       /* this rank's flag words */
   int64_t timeout_ns;
   int32_t* err_word;     /* optional DEVICE int32 for this rank's flags; NULL = library-wide word */
-  int32_t acc16;         /* 0: the switch sums in fp32 and rounds once (default); 1: it sums in the
-                            16-bit type (as a ring all-reduce in that type rounds at every hop) */
 } mlora_mc_ar;
 int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int64_t row_end, int32_t slot, void* stream);
 int mlora_mc_wait(const mlora_mc_ar* ar, int32_t n_slots, void* stream);

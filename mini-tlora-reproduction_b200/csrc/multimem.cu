@@ -63,7 +63,7 @@ struct McReduce {
   int64_t u0, u1;         // 16-byte units of Y this rank sums: [u0, u1)
   unsigned world;
   unsigned long long timeout_ns;
-  int slot, f16, acc16;
+  int slot, f16;
   int* err;
 };
 
@@ -113,21 +113,9 @@ __global__ void k_mc_signal(uint32_t* flags_mc, uint32_t* flags, int slot) {
   }
 }
 
-__device__ __forceinline__ uint4 mc_ld_reduce(const uint8_t* p, int f16, int acc16) {
+__device__ __forceinline__ uint4 mc_ld_reduce(const uint8_t* p, int f16) {
   uint4 v;
-  if (acc16) {  // the switch sums in the 16-bit type
-    if (f16) {
-      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f16x2 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                   : "l"(p)
-                   : "memory");
-    } else {
-      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                   : "l"(p)
-                   : "memory");
-    }
-  } else if (f16) {
+  if (f16) {
     asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p)
@@ -162,11 +150,11 @@ __global__ void __launch_bounds__(kMcThreads) k_mc_reduce(const __grid_constant_
     for (; u + (kMcUnroll - 1) * stride < a.u1; u += kMcUnroll * stride) {
       uint4 v[kMcUnroll];
 #pragma unroll
-      for (int q = 0; q < kMcUnroll; ++q) v[q] = mc_ld_reduce(a.y_mc + (u + q * stride) * 16, a.f16, a.acc16);
+      for (int q = 0; q < kMcUnroll; ++q) v[q] = mc_ld_reduce(a.y_mc + (u + q * stride) * 16, a.f16);
 #pragma unroll
       for (int q = 0; q < kMcUnroll; ++q) mc_st(a.y_mc + (u + q * stride) * 16, v[q]);
     }
-    for (; u < a.u1; u += stride) mc_st(a.y_mc + u * 16, mc_ld_reduce(a.y_mc + u * 16, a.f16, a.acc16));
+    for (; u < a.u1; u += stride) mc_st(a.y_mc + u * 16, mc_ld_reduce(a.y_mc + u * 16, a.f16));
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -226,7 +214,6 @@ extern "C" int mlora_mc_allreduce(const mlora_mc_ar* ar, int64_t row_begin, int6
   a.timeout_ns = mc_timeout(ar);
   a.slot = slot;
   a.f16 = ar->dtype == MLORA_F16 ? 1 : 0;
-  a.acc16 = ar->acc16 ? 1 : 0;
   a.err = ar->err_word;
   int dev = 0, sms = 0;
   MLORA_CUDA_TRY(cudaGetDevice(&dev));

@@ -120,7 +120,6 @@ class McAr(ctypes.Structure):
         ("flags", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_int64),
         ("err_word", ctypes.c_void_p),
-        ("acc16", ctypes.c_int32),
     ]
 
 
