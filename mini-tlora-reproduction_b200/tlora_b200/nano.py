@@ -32,6 +32,20 @@ def split_ranges(total: int, n: int) -> List[Tuple[int, int]]:
 split_into_n = split_ranges
 
 
+def ramp_ranges(total: int, n: int, first: float = 0.5) -> List[Tuple[int, int]]:
+    """N contiguous ranges over ``total`` units whose first range is ``first``
+    times the size of the others (each at least one unit): a short first
+    nano-batch starts the all-reduce chain earlier.  N is clamped as in
+    split_ranges; with N = 1 the whole range."""
+    if total <= 0:
+        return [(0, 0)]
+    n = min(max(1, int(n)), total)
+    if n == 1:
+        return [(0, total)]
+    head = max(1, min(total - (n - 1), int(round(total * first / (first + n - 1)))))
+    return [(0, head)] + [(head + s, head + e) for s, e in split_ranges(total - head, n - 1)]
+
+
 class AIMDController:
     """Additive-increase / multiplicative-decrease control of the nano-batch
     count N from measured iteration times.

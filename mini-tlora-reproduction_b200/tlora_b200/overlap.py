@@ -58,7 +58,7 @@ import torch.distributed as dist
 
 from . import _lib, ops, peer
 from ._lib import TILE_ROWS
-from .nano import split_ranges
+from .nano import ramp_ranges, split_ranges
 
 COMMS = ("nccl", "peer", "mc")
 
@@ -244,6 +244,10 @@ class ShardedLayer:
         if dz not in ("split", "replicated"):
             raise ValueError(f"dz must be 'split' or 'replicated', not {dz!r}")
         self.dz = dz
+        # nano-batch ranges over the plan tiles: "even" (the reference's
+        # split_ranges) or "ramp" (the first nano-batch half as long, so that
+        # the all-reduce chain starts earlier)
+        self.split = "even"
         self.rank, self.world, self.group = rank, world, group
         self.comm = comm
         self.err_word = err_word
@@ -289,6 +293,12 @@ class ShardedLayer:
         torch.cuda.synchronize()
         t0 = self.timeline[0][1]
         return {name: round(t0.elapsed_time(ev), 4) for name, ev in self.timeline}
+
+    def ranges(self, n_tiles: int, n_nano: int):
+        """The nano-batches' plan-tile ranges (see ``split``)."""
+        if self.split == "ramp":
+            return ramp_ranges(n_tiles, n_nano)
+        return split_ranges(n_tiles, n_nano)
 
     def check(self) -> None:
         """Raise if a kernel of this layer flagged a device-side check (reads
@@ -353,7 +363,7 @@ class ShardedLayer:
             hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
         rows = x_p.shape[0]
         works = []
-        for i, (t0, t1) in enumerate(split_ranges(ctx["n_tiles"], n_nano)):
+        for i, (t0, t1) in enumerate(self.ranges(ctx["n_tiles"], n_nano)):
             own = self._owner(i)
             if own and hz is not None:
                 hz.wait()  # the expand reads the summed Z
@@ -427,7 +437,7 @@ class ShardedLayer:
         if ctx["z"] is not None:
             hz = dist.all_reduce(ctx["z"], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
         side = self._side
-        ranges = split_ranges(ctx["n_tiles"], n_nano)
+        ranges = self.ranges(ctx["n_tiles"], n_nano)
         for i, (t0, t1) in enumerate(ranges):
             own = self._owner(i)
             if own and hz is not None:
@@ -619,7 +629,7 @@ def comm_only(layer: ShardedLayer, y: torch.Tensor, z: Optional[torch.Tensor], n
     if z is not None:
         works.append(dist.all_reduce(z, op=dist.ReduceOp.SUM, group=layer.group, async_op=True))
     rows = y.shape[0]
-    ranges = split_ranges(n_tiles, n_nano)
+    ranges = layer.ranges(n_tiles, n_nano)
     if layer.comm == "mc" and layer._mc is not None and y.data_ptr() == layer._mc.y.data_ptr():
         mc = layer._mc
         cur = torch.cuda.current_stream(y.device)

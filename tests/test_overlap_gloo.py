@@ -120,13 +120,14 @@ def _build(seed=0):
     return m, ids, x, dy
 
 
-def _worker(rank, world, port, n_nano, pipelined, q, dz="split"):
+def _worker(rank, world, port, n_nano, pipelined, q, dz="split", split="even"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         m, ids, x, dy = _build()
         layer = ShardedLayer(m, rank, world, compute=DenseCompute(), bwd_group=dist.new_group(list(range(world))),
                              dz=dz)
+        layer.split = split
         plan = ops.route(ids, layer.table, torch.device("cpu"))
         x_p = layer.shard_input(x)
         y, dx_p = layer.step(x_p, plan, dy, n_nano, lr=0.01, pipelined=pipelined)
@@ -143,17 +144,22 @@ def _worker(rank, world, port, n_nano, pipelined, q, dz="split"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n_nano,pipelined,dz", [(2, 1, True, "split"), (2, 3, True, "split"),
-                                                       (2, 2, False, "split"), (3, 4, True, "split"),
-                                                       (1, 2, True, "split"), (2, 3, True, "replicated"),
-                                                       (3, 2, True, "replicated")])
-def test_sharded_step_matches_unsharded(world, n_nano, pipelined, dz):
+@pytest.mark.parametrize("world,n_nano,pipelined,dz,split", [(2, 1, True, "split", "even"), (2, 3, True, "split", "even"),
+                                                             (2, 2, False, "split", "even"),
+                                                             (3, 4, True, "split", "even"),
+                                                             (1, 2, True, "split", "even"),
+                                                             (2, 3, True, "replicated", "even"),
+                                                             (3, 2, True, "replicated", "even"),
+                                                             (2, 3, True, "split", "ramp")])
+def test_sharded_step_matches_unsharded(world, n_nano, pipelined, dz, split):
     """Every rank's step against the fp64 oracle of the unsharded layer; dZ
-    split across the ranks and summed, or computed whole on every rank."""
+    split across the ranks and summed, or computed whole on every rank; even
+    nano-batches or a short first one."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, pipelined, q, dz)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, pipelined, q, dz, split))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = q.get(timeout=120)
@@ -186,6 +192,19 @@ def test_shard_columns_cover_exactly():
             assert spans[0][0] == 0 and spans[-1][1] == d
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
             assert all(s % 64 == 0 for s, _ in spans)
+
+
+def test_ramp_ranges_cover_exactly():
+    from tlora_b200.nano import ramp_ranges
+    for total in (1, 2, 5, 39, 153):
+        for n in (1, 2, 3, 4, 8, 16):
+            r = ramp_ranges(total, n)
+            assert r[0][0] == 0 and r[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+            assert all(e > s for s, e in r)
+            assert len(r) == min(n, total)
+            if len(r) > 2:
+                assert r[0][1] - r[0][0] <= min(e - s for s, e in r[1:])
 
 
 def test_nano_ranges_over_tiles():
