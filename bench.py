@@ -417,6 +417,7 @@ def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes
                                for n in (r, d_in, d_out, r))
     want = reference_probes(w, probes)
     errs_a, errs_b, sgd_ok = [], [], True
+    sgd_bad = {"A": 0, "B": 0}  # elements outside the bound, per tensor
     k0, k1 = layer.k0, layer.k1
     for i in range(layer.table.n):
         a = str(layer.table.ids[i])
@@ -433,11 +434,13 @@ def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes
         errs_a.append(_rel(pa, want[a][0]))
         errs_b.append(_rel(pb, want[a][1]))
         # P' = bf16(P - lr G): within 2^-8 relative (half a bf16 ulp, doubled)
-        for P1, P0, G in ((layer.A_pack[o:o + r], A0[o:o + r], dA_p[o:o + r]),
-                          (layer.B_pack[:, o:o + r], B0[:, o:o + r], dB[:, o:o + r])):
+        for name, P1, P0, G in (("A", layer.A_pack[o:o + r], A0[o:o + r], dA_p[o:o + r]),
+                                ("B", layer.B_pack[:, o:o + r], B0[:, o:o + r], dB[:, o:o + r])):
             exp = P0.double() - w.spec.lr * G.double()
             bound = 2.0 ** -8 * exp.abs() + 1e-6 * (P0.double().abs() + w.spec.lr * G.double().abs()) + 1e-30
-            sgd_ok = sgd_ok and bool(((P1.double() - exp).abs() <= bound).all())
+            bad = int(((P1.double() - exp).abs() > bound).sum())
+            sgd_bad[name] += bad
+            sgd_ok = sgd_ok and bad == 0
     out["dA"] = max(errs_a) if errs_a else 0.0
     out["dB"] = max(errs_b) if errs_b else 0.0
     ok = torch.tensor([1.0 if sgd_ok else 0.0], device=dev)
@@ -447,6 +450,10 @@ def ksharded_parity(layer, w, x_p, plan, n_nano, world, dev, n_rows=64, n_probes
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out["Y"], out["dA"], out["dB"] = (float(v) for v in t.tolist())
     out["sgd_elementwise_ok"] = bool(ok.item() > 0)
+    bad = torch.tensor([sgd_bad["A"], sgd_bad["B"]], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+    out["sgd_elements_outside"] = {"A": int(bad[0].item()), "B": int(bad[1].item())}
     res = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in out.items()}
     res["tol"] = TOL
     res["ok"] = all(out[k] <= TOL for k in ("Y", "dX", "dA", "dB")) and out["sgd_elementwise_ok"]
