@@ -575,9 +575,10 @@ def run_path(layer, w, x_p, plan, comm, args, dev, world):
     graphs = {}
 
     def graphed(n, comm_on=True):
-        if (n, comm_on) not in graphs:
-            graphs[(n, comm_on)] = GraphedShardedStep(layer, x_p, plan, dy, n, lr, comm=comm_on)
-        return graphs[(n, comm_on)]
+        key = (n, comm_on, layer.split)
+        if key not in graphs:
+            graphs[key] = GraphedShardedStep(layer, x_p, plan, dy, n, lr, comm=comm_on)
+        return graphs[key]
 
     def stepper(n, pipelined=True, comm_on=True):
         return lambda: layer.step(x_p, plan, dy, n, lr, pipelined, comm_on)
@@ -602,10 +603,21 @@ def run_path(layer, w, x_p, plan, comm, args, dev, world):
             res["n_sweep_ms"] = {str(k): round(v, 4) for k, v in sweep.items()}
             res["aimd"] = horizons
             res["aimd_best_n"] = ctl.best_n
+            # the reference's even nano-batches against a first one half as long
+            # (starts the all-reduce chain earlier), at the chosen N
+            if best_n > 1:
+                layer.split = "ramp"
+                t_ramp = timed_med(graphed(best_n), 3, dev, world)
+                layer.split = "even"
+                t_even = timed_med(graphed(best_n), 3, dev, world)
+                res["split_ms"] = {"even": round(t_even, 4), "ramp": round(t_ramp, 4)}
+                if t_ramp < t_even:
+                    layer.split = "ramp"
         else:
             best_n = 1
         ms = timed_med(graphed(best_n), args.steps, dev, world)
         res["n"] = best_n
+        res["split"] = layer.split
         res["ms_per_step"] = round(ms, 4)
         launches0 = _lib.launch_count()
         eager_ms, host_ms = host_and_device(stepper(best_n), args.steps, dev, world)
@@ -630,6 +642,7 @@ def run_path(layer, w, x_p, plan, comm, args, dev, world):
     finally:
         torch.cuda.synchronize(dev)
         graphs.clear()  # before the layer's buffers are released
+        layer.split = "even"
     return res
 
 
@@ -746,6 +759,7 @@ def run_ours(args, peaks_d, peaks_kind):
         bres = good[best]
         n = bres["n"]
         layer.comm = best
+        layer.split = split = bres.get("split", "even")
 
         # clocks and launch count over a timed region of the chosen path
         clocks = ClockSampler(dev.index) if rank == 0 else None
@@ -799,6 +813,7 @@ def run_ours(args, peaks_d, peaks_kind):
             "config": ksharded_config(sp, world),
             "allreduce": best if world > 1 else None,
             "nano_batches": n,
+            "nano_split": split,
             "step_tflops": round(sp.flops() / (ms / 1000.0) / 1e12, 1),
             "step_frac_of_peak": round(sp.flops() / world / (ms / 1000.0) / 1e12 / float(peaks_d["bf16_tflops"]), 4),
             "roofline": roof,
