@@ -45,7 +45,7 @@ def _spec():
     return workloads.spec("c3", scale=0.125)
 
 
-def run_rank(rank, world, n_nano, dev, steps=1):
+def run_rank(rank, world, n_nano, dev, steps=1, split="even", dz="split"):
     """One rank's training step(s); returns numpy Y, this rank's dX shard,
     dA shard, dB, the updated A shard and B, and the shard's columns."""
     from tlora_b200 import _lib, ops, workloads
@@ -54,7 +54,8 @@ def run_rank(rank, world, n_nano, dev, steps=1):
     w = workloads.build(_spec(), device=dev)
     group = dist.new_group(list(range(world))) if world > 1 else None
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    layer = ShardedLayer(w.model, rank, world, bwd_group=group, err_word=err)
+    layer = ShardedLayer(w.model, rank, world, bwd_group=group, err_word=err, dz=dz)
+    layer.split = split
     plan = ops.route(w.ids.cpu(), layer.table, dev)
     x_p = layer.shard_input(w.x)
     for _ in range(steps):
@@ -116,10 +117,11 @@ def check_against_oracle(parts, steps=1):
     return errs
 
 
-@pytest.mark.parametrize("n_nano", [1, 3])
-def test_one_rank_pipeline_matches_oracle(n_nano):
-    """The pipeline's one-GPU point: no collective at all."""
-    res = run_rank(0, 1, n_nano, torch.device("cuda", 0))
+@pytest.mark.parametrize("n_nano,split", [(1, "even"), (3, "even"), (3, "ramp")])
+def test_one_rank_pipeline_matches_oracle(n_nano, split):
+    """The pipeline's one-GPU point: no collective at all; even nano-batches
+    or a short first one."""
+    res = run_rank(0, 1, n_nano, torch.device("cuda", 0), split=split)
     check_against_oracle([res])
 
 
@@ -155,24 +157,25 @@ def test_graphed_step_matches_eager_step(n_nano):
     assert g.kernels > 0
 
 
-def _worker(rank, world, port, n_nano, q):
+def _worker(rank, world, port, n_nano, q, split="even", dz="split"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
-        q.put((rank, run_rank(rank, world, n_nano, dev)))
+        q.put((rank, run_rank(rank, world, n_nano, dev, split=split, dz=dz)))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n_nano", [(2, 1), (2, 3), (3, 4)])
-def test_sharded_ranks_on_one_gpu_match_oracle(world, n_nano):
+@pytest.mark.parametrize("world,n_nano,split,dz", [(2, 1, "even", "split"), (2, 3, "even", "split"),
+                                                   (3, 4, "even", "split"), (2, 3, "ramp", "replicated")])
+def test_sharded_ranks_on_one_gpu_match_oracle(world, n_nano, split, dz):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_nano, q, split, dz)) for r in range(world)]
     for p in procs:
         p.start()
     parts = {}
