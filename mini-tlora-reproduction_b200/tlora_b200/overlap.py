@@ -682,6 +682,16 @@ class GraphedShardedStep:
         layer._last_done = None
         layer._pending = None
         self.grads = layer.last_grads
+        # Every buffer the captured kernels and collectives read or write
+        # must live as long as the graph, also after the layer replaces its
+        # cached objects (a later step with comm off, other inputs or another
+        # plan builds new call arguments, workspaces, gradient buffers and SGD
+        # item lists; without these references the old ones would go back to
+        # the allocator while the graph still points at them).  close() of the
+        # layer releases the peer / multicast buffers and ends the graph's use.
+        c = layer.compute
+        self._keep = (getattr(c, "_fw", None), getattr(c, "_bw", None), getattr(c, "_sgd", None),
+                      layer._one, layer._ar, layer._mc, layer._side, plan, x_p, dy)
 
     def __call__(self):
         """Replay one step on the current stream; returns (Y, dX_p)."""

@@ -157,6 +157,46 @@ def test_graphed_step_matches_eager_step(n_nano):
     assert g.kernels > 0
 
 
+def test_graph_outlives_the_layers_cached_buffers():
+    """A captured step keeps its buffers after the layer rebuilds its cached
+    call objects (here: a step with another plan object) and their old
+    memory is handed out again: replays still give the eager step's results
+    bit for bit."""
+    from tlora_b200 import ops, workloads
+    from tlora_b200.overlap import GraphedShardedStep, ShardedLayer
+
+    dev = torch.device("cuda", 0)
+    w = workloads.build(_spec(), device=dev)
+    layer = ShardedLayer(w.model, 0, 1)
+    plan = ops.route(w.ids.cpu(), layer.table, dev)
+    x_p = layer.shard_input(w.x)
+    A0, B0 = layer.A_pack.clone(), layer.B_pack.clone()
+    g = GraphedShardedStep(layer, x_p, plan, w.dy, 3, w.spec.lr)
+
+    def reset():
+        with torch.no_grad():
+            layer.A_pack.copy_(A0)
+            layer.B_pack.copy_(B0)
+
+    reset()
+    y, dx = layer.step(x_p, plan, w.dy, 3, w.spec.lr)
+    want = [t.clone() for t in (y, dx, *layer.last_grads, layer.A_pack, layer.B_pack)]
+    # another plan object: the layer builds new call objects and buffers
+    plan2 = ops.route(w.ids.cpu(), layer.table, dev)
+    reset()
+    layer.step(x_p, plan2, w.dy, 3, w.spec.lr)
+    torch.cuda.synchronize(dev)
+    # take back whatever the allocator has free and scribble on it
+    junk = [torch.full((1 << 20,), 7, dtype=torch.int32, device=dev) for _ in range(64)]
+    reset()
+    y, dx = g()
+    got = [t.clone() for t in (y, dx, *g.grads, layer.A_pack, layer.B_pack)]
+    torch.cuda.synchronize(dev)
+    del junk
+    for name, a, b in zip(("Y", "dX", "dA", "dB", "A", "B"), got, want):
+        assert torch.equal(a, b), name
+
+
 def _worker(rank, world, port, n_nano, q, split="even", dz="split"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
