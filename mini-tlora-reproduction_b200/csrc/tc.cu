@@ -34,7 +34,8 @@
 //    a 256x512 tile, two M = 256, N = 256 MMAs per k-block into one
 //    512-column accumulator drained in two halves (48 KB per stage, 4
 //    stages); bit-identical to k_tc2, a comparison path.
-//  * k_tc (SHRINK_*, REDUCE, and the 1-SM variant of the mainloops): one CTA,
+//  * k_tc (SHRINK_*, REDUCE, the forward mainloop below d_in = 2048 and the
+//    all-1-SM comparison path): one CTA,
 //    M = 128, N <= 256, a 216 KB ring cut per launch (4 stages of 48 KB for a
 //    mainloop, up to 9 narrower stages for the HBM-bound roles).
 //
@@ -70,7 +71,8 @@ namespace {
 // one issuing warp whatever the ring depth, 64 GB/s with two and 118 GB/s
 // with four), which held the mainloops below the tensor pipe's rate.
 // Three or four producer warps measured the same as two (mainloops within
-// ±3 %, the reduction 5 % faster at c3 and 3 % slower at c2).
+// ±3 %; the reduction 5 % faster on an 8192 x 8192 layer with 32 adapters and
+// 3 % slower on a 4096 -> 11008 layer with 8).
 constexpr int kProducers = 2;  // warp 0 and warps 6 .. 6 + kProducers - 2
 constexpr int kThreads = 32 * (6 + kProducers - 1);
 constexpr int kBox64 = 64 * 64 * 2;  // one 64x64 bf16 box, 8 KB
@@ -1767,7 +1769,7 @@ int launch2w(TcParams& prm, cudaStream_t st, int max_ctas, bool pdl = false) {
 
 // Raster of a main launch with n_m 256-row tiles x n_n N blocks of `width`
 // columns and K-extent k (16-bit; an A tile is 256 x k, a B block width x k).  Measured on B200
-// (c2 shapes, a sweep of orientations and group sizes on one box): the 1-SM
+// (65,536 x 4096 -> 11008, a sweep of orientations and group sizes on one box): the 1-SM
 // mainloop is fastest with groups of M tiles sweeping N, the 2-SM mainloop
 // with groups of N blocks sweeping M, both with about 48 MB of the
 // group's stationary operand (4..16 tiles or blocks).
