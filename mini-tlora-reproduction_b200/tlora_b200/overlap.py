@@ -295,9 +295,12 @@ class ShardedLayer:
         return {name: round(t0.elapsed_time(ev), 4) for name, ev in self.timeline}
 
     def ranges(self, n_tiles: int, n_nano: int):
-        """The nano-batches' plan-tile ranges (see ``split``)."""
-        if self.split == "ramp":
-            return ramp_ranges(n_tiles, n_nano)
+        """The nano-batches' plan-tile ranges (see ``split``; "ramp:<f>" sets
+        the first nano-batch's length relative to the others, 0.5 for
+        "ramp")."""
+        if self.split.startswith("ramp"):
+            first = float(self.split.split(":")[1]) if ":" in self.split else 0.5
+            return ramp_ranges(n_tiles, n_nano, first)
         return split_ranges(n_tiles, n_nano)
 
     def check(self) -> None:
