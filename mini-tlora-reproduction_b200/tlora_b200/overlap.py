@@ -298,10 +298,14 @@ class ShardedLayer:
         """The nano-batches' plan-tile ranges (see ``split``; "ramp:<f>" sets
         the first nano-batch's length relative to the others, 0.5 for
         "ramp")."""
-        if self.split.startswith("ramp"):
-            first = float(self.split.split(":")[1]) if ":" in self.split else 0.5
+        if self.split == "even":
+            return split_ranges(n_tiles, n_nano)
+        if self.split == "ramp" or self.split.startswith("ramp:"):
+            first = float(self.split[5:]) if ":" in self.split else 0.5
+            if not first > 0:
+                raise ValueError(f"the first nano-batch's relative length must be > 0: {self.split!r}")
             return ramp_ranges(n_tiles, n_nano, first)
-        return split_ranges(n_tiles, n_nano)
+        raise ValueError(f"split must be 'even', 'ramp' or 'ramp:<fraction>', not {self.split!r}")
 
     def check(self) -> None:
         """Raise if a kernel of this layer flagged a device-side check (reads
