@@ -194,6 +194,19 @@ def test_shard_columns_cover_exactly():
             assert all(s % 64 == 0 for s, _ in spans)
 
 
+def test_split_setting_is_checked():
+    from tlora_b200.overlap import ShardedLayer
+    m, _, _, _ = _build()
+    layer = ShardedLayer(m, 0, 1, compute=DenseCompute())
+    assert layer.ranges(10, 3) == [(0, 4), (4, 7), (7, 10)]
+    layer.split = "ramp:0.25"
+    assert layer.ranges(153, 4)[0] == (0, 12)
+    for bad in ("bogus", "ramp:0", "ramp:-1"):
+        layer.split = bad
+        with pytest.raises(ValueError):
+            layer.ranges(10, 3)
+
+
 def test_ramp_ranges_cover_exactly():
     from tlora_b200.nano import ramp_ranges
     for total in (1, 2, 5, 39, 153):
